@@ -1,0 +1,95 @@
+// abi.cu - C-ABI utilities: versions, status strings, device info, PDL launch,
+// the device error flag written by kernels that gave up a bounded wait.
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "dbk_internal.h"
+
+namespace dbk {
+
+__device__ int dbk_device_error = 0;
+
+namespace {
+constexpr int kMaxDevices = 64;
+DeviceInfo g_info[kMaxDevices];
+bool g_have[kMaxDevices];
+std::mutex g_mu;
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("DBK_PDL");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+}  // namespace
+
+int current_device_info(DeviceInfo* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevices) return DBK_EDEVICE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_have[dev]) {
+    DeviceInfo d{};
+    d.device = dev;
+    if ((e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev))) return (int)e;
+    if ((e = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)))
+      return (int)e;
+    if ((e = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev))) return (int)e;
+    g_info[dev] = d;
+    g_have[dev] = true;
+  }
+  if (g_info[dev].cc_major != 10) return DBK_EDEVICE;
+  *out = g_info[dev];
+  return DBK_OK;
+}
+
+int launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               void* args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  void* params[1] = {args};
+  cudaError_t e = cudaLaunchKernelExC(&cfg, func, params);
+  return e == cudaSuccess ? DBK_OK : (int)e;
+}
+
+}  // namespace dbk
+
+extern "C" int dbk_abi_version(void) { return DBK_ABI_VERSION; }
+
+extern "C" const char* dbk_status_string(int s) {
+  switch (s) {
+    case DBK_OK: return "ok";
+    case DBK_ENULL: return "a required pointer is NULL";
+    case DBK_ESHAPE: return "a size is outside the supported range";
+    case DBK_EALIGN: return "a pointer or row stride is not 16-byte aligned";
+    case DBK_EWORKSPACE: return "workspace missing or too small";
+    case DBK_EDTYPE: return "unknown dtype";
+    case DBK_EDEVICE: return "current device is not an sm_100 (B200) GPU";
+    default: break;
+  }
+  if (s > 0) return cudaGetErrorString(static_cast<cudaError_t>(s));
+  return "unknown status";
+}
+
+extern "C" int dbk_take_device_error(void) {
+  int v = 0, zero = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return (int)e;
+  e = cudaMemcpyFromSymbol(&v, dbk::dbk_device_error, sizeof(int));
+  if (e != cudaSuccess) return (int)e;
+  e = cudaMemcpyToSymbol(dbk::dbk_device_error, &zero, sizeof(int));
+  if (e != cudaSuccess) return (int)e;
+  return v;
+}

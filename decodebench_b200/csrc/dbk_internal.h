@@ -1,0 +1,43 @@
+// dbk_internal.h - host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "dbk.h"
+
+namespace dbk {
+
+// Largest batch served by the CUDA-core GEMV path; larger batches use tcgen05.
+constexpr int kSimtMaxBatch = 8;
+
+struct DeviceInfo {
+  int device;
+  int num_sms;
+  int max_smem_optin;
+  int cc_major;
+};
+
+// Cached per-device properties of the current device; DBK_EDEVICE if not sm_100.
+int current_device_info(DeviceInfo* out);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launch `func(*args)` (one by-value struct parameter) with programmatic
+// dependent launch enabled unless DBK_PDL=0 is set in the environment.
+int launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               void* args);
+
+}  // namespace dbk
+
+// Tensor-core (tcgen05) paths for batch > kSimtMaxBatch, defined in gemm_tc.cu.
+int dbk_tc_rmsnorm_gemv(const void* x, const void* gamma, const void* W, void* y, int batch,
+                        int d_in, int d_out, float eps, int dtype, void* ws, size_t ws_bytes,
+                        void* stream);
+int dbk_tc_gateup_swiglu(const void* x, const void* gamma, const void* Wg, const void* Wu,
+                         void* h, int batch, int d_in, int d_ff, float eps, int dtype, void* ws,
+                         size_t ws_bytes, void* stream);
+int dbk_tc_gemv(const void* x, const void* W, const void* residual, void* y, int batch,
+                int d_in, int d_out, int dtype, void* ws, size_t ws_bytes, void* stream);
+size_t dbk_tc_workspace_bytes(int op, int64_t batch, int64_t d_in, int64_t d_out);

@@ -1,0 +1,368 @@
+// gemv.cu - batch-1..8 decode GEMV family on CUDA cores, weights streamed by TMA.
+//
+// One kernel template serves three fused operations:
+//   MODE_PLAIN    y = W x (+ residual)                       (down projection)
+//   MODE_NORM     y = inv_rms * W (x * gamma)                 (F1: RMSNorm -> GEMV)
+//   MODE_SWIGLU   h = silu(Wg x') * (Wu x'), x' = x or the    (F2: gate+up -> SwiGLU)
+//                 RMSNorm of x when gamma is given
+//
+// Design (B200): the op is a pure HBM stream of W (2 bytes per weight, 1..8 FMAs
+// per weight), so the kernel is built to keep ~190 KB of weight bytes in flight
+// per SM from the first cycle:
+//   * one persistent CTA per SM owns a contiguous block of output rows;
+//   * a producer warp walks the CTA's weight rows in K-chunks and issues one
+//     cp.async.bulk (TMA, non-tensor) per (row, chunk) segment into a ring of
+//     32 KB shared-memory stages tracked by mbarriers (L2 evict-first policy);
+//   * eight consumer warps each own the weight rows i = w (mod 8) of the CTA, so
+//     per-row accumulation order is fixed (deterministic results); a lane keeps
+//     the activation chunk it needs in registers (x*gamma in fp32), reads 16-byte
+//     vectors of W from shared memory, and a warp reduction adds each segment's
+//     partial dot to the row's fp32 accumulator in shared memory;
+//   * RMSNorm is not a separate pass: inv_rms is a per-batch-row scalar, so
+//     W (x * gamma * inv_rms) = inv_rms * W (x * gamma); the consumers compute
+//     sum(x^2) while the producer's first copies are in flight and apply
+//     inv_rms in the epilogue, where SwiGLU and the residual add are fused too.
+//   * programmatic dependent launch: the weight stream starts before
+//     griddepcontrol.wait; activations are read and outputs written after it.
+//
+// Reference semantics: fused f1_kernel / f2_kernel
+// (validation/src/kernels/fused/f1.cu:18-84, f2.cu:17-76) and the Python stages
+// (src/decodebench/demos/llama_decode.py:36-43, :77-87): fp32 accumulation,
+// silu(g) = g / (1 + exp(-g)) (f2.cu:73), output rounded once to fp16/bf16.
+#include "common.cuh"
+#include "dbk_internal.h"
+
+namespace dbk {
+namespace {
+
+enum GemvMode : int { MODE_PLAIN = 0, MODE_NORM = 1, MODE_SWIGLU = 2 };
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;   // + one producer warp
+constexpr int kStageBytes = 32 * 1024;
+constexpr int kMaxStages = 6;
+
+struct GemvArgs {
+  const void* x;         // [batch, d_in]
+  const void* gamma;     // [d_in] or nullptr
+  const void* w0;        // [d_out, d_in]   (W, or Wg)
+  const void* w1;        // [d_out, d_in]   (Wu) for MODE_SWIGLU
+  const void* residual;  // [batch, d_out] or nullptr
+  void* y;               // [batch, d_out]
+  int batch, d_in, d_out;
+  float eps;
+  int kc;                // columns per (row, chunk) segment
+  int nchunks;           // ceil(d_in / kc)
+  int slots;             // segments per stage (multiple of 8)
+  int nstages;           // ring depth
+  int max_rows;          // max output rows of any CTA
+};
+
+// Shared-memory carve-up (dynamic): ring | full[] | empty[] | acc | inv_rms
+struct Smem {
+  uint8_t* ring;
+  uint64_t* full;
+  uint64_t* empty;
+  float* acc;      // [max_rows * nmat][NB]
+  float* inv_rms;  // [NB]
+};
+
+__device__ __forceinline__ Smem carve(uint8_t* base, const GemvArgs& a, int nmat, int nb) {
+  Smem s;
+  s.ring = base;
+  s.full = reinterpret_cast<uint64_t*>(base + (size_t)a.nstages * kStageBytes);
+  s.empty = s.full + a.nstages;
+  s.acc = reinterpret_cast<float*>(s.empty + a.nstages);
+  s.inv_rms = s.acc + (size_t)a.max_rows * nmat * nb;
+  return s;
+}
+
+template <typename T, int NB, int MODE, int KCG>
+__global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(const GemvArgs a) {
+  constexpr int NMAT = (MODE == MODE_SWIGLU) ? 2 : 1;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Smem sm = carve(smem_raw, a, NMAT, NB);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x;
+  const int row0 = (int)(((int64_t)blockIdx.x * a.d_out) / G);
+  const int row1 = (int)(((int64_t)(blockIdx.x + 1) * a.d_out) / G);
+  const int nrows = row1 - row0;
+  const int nwr = nrows * NMAT;                       // weight rows of this CTA
+  const int spc = (nwr + a.slots - 1) / a.slots;      // stages per chunk
+  const int total = spc * a.nchunks;
+  const int slot_bytes = a.kc * (int)sizeof(T);
+
+  if (tid == 0) {
+    for (int s = 0; s < a.nstages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  // Let the next kernel in the stream start its own weight stream early.
+  asm volatile("griddepcontrol.launch_dependents;");
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const T* W[2] = {static_cast<const T*>(a.w0), static_cast<const T*>(a.w1)};
+      for (int j = 0; j < total; ++j) {
+        const int s = j % a.nstages;
+        if (j >= a.nstages &&
+            !mbar_wait(&sm.empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty))
+          return;
+        const int k = j / spc;
+        const int i0 = (j % spc) * a.slots;
+        const int n = min(a.slots, nwr - i0);
+        const int col0 = k * a.kc;
+        const int seg = min(a.kc, a.d_in - col0);
+        mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(n * seg * sizeof(T)));
+        uint8_t* dst = sm.ring + (size_t)s * kStageBytes;
+        for (int q = 0; q < n; ++q) {
+          const int i = i0 + q;
+          const int r = row0 + i / NMAT;
+          const T* src = W[i % NMAT] + (size_t)r * a.d_in + col0;
+          bulk_g2s(dst + q * slot_bytes, src, (uint32_t)(seg * sizeof(T)), &sm.full[s], pol);
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  // Activations may be produced by the previous kernel in the stream.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const T* x = static_cast<const T*>(a.x);
+  const T* gam = static_cast<const T*>(a.gamma);
+
+  for (int idx = tid; idx < a.max_rows * NMAT * NB; idx += kConsumers) sm.acc[idx] = 0.f;
+  if constexpr (MODE != MODE_PLAIN) {
+    if (gam != nullptr) {
+      // sum(x^2) per batch row: every CTA recomputes it (x is a few KB, L2-resident).
+      __shared__ float red[kConsumerWarps][NB];
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        float ss = 0.f;
+        if (b < a.batch) {
+          for (int c = tid * 8; c < a.d_in; c += kConsumers * 8) {
+            float f[8];
+            unpack8<T>(ldg_nc_v4(x + (size_t)b * a.d_in + c), f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+          }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp][b] = ss;
+      }
+      named_bar_sync(1, kConsumers);
+      if (tid < NB) {
+        float ss = 0.f;
+        for (int w = 0; w < kConsumerWarps; ++w) ss += red[w][tid];
+        sm.inv_rms[tid] = rsqrtf(ss / (float)a.d_in + a.eps);
+      }
+    } else if (tid < NB) {
+      sm.inv_rms[tid] = 1.f;
+    }
+  }
+  named_bar_sync(1, kConsumers);
+
+  float xr[NB][KCG][8];
+  int cur_k = -1;
+  for (int j = 0; j < total; ++j) {
+    const int s = j % a.nstages;
+    const int k = j / spc;
+    const int i0 = (j % spc) * a.slots;
+    const int n = min(a.slots, nwr - i0);
+    const int col0 = k * a.kc;
+    const int seg = min(a.kc, a.d_in - col0);
+    if (k != cur_k) {   // new K-chunk: load x (* gamma) for this lane's columns
+      cur_k = k;
+#pragma unroll
+      for (int g = 0; g < KCG; ++g) {
+        const int c = (lane + 32 * g) * 8;
+        float gm[8];
+        if (gam != nullptr && c < seg) unpack8<T>(ldg_nc_v4(gam + col0 + c), gm);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          if (b < a.batch && c < seg) {
+            unpack8<T>(ldg_nc_v4(x + (size_t)b * a.d_in + col0 + c), xr[b][g]);
+            if (gam != nullptr) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) xr[b][g][e] *= gm[e];
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xr[b][g][e] = 0.f;
+          }
+        }
+      }
+    }
+    if (!mbar_wait(&sm.full[s], (j / a.nstages) & 1, kDevTimeoutFull)) return;
+    const uint32_t stage = smem_u32(sm.ring + (size_t)s * kStageBytes);
+    for (int q = warp; q < n; q += kConsumerWarps) {
+      float part[NB];
+#pragma unroll
+      for (int b = 0; b < NB; ++b) part[b] = 0.f;
+#pragma unroll
+      for (int g = 0; g < KCG; ++g) {
+        const int c = (lane + 32 * g) * 8;
+        if (c < seg) {
+          float wf[8];
+          unpack8<T>(ld_shared_v4(stage + q * slot_bytes + c * (int)sizeof(T)), wf);
+#pragma unroll
+          for (int b = 0; b < NB; ++b)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) part[b] = fmaf(wf[e], xr[b][g][e], part[b]);
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < NB; ++b) part[b] = warp_sum(part[b]);
+      if (lane == 0) {
+        float* acc = sm.acc + (size_t)(i0 + q) * NB;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) acc[b] += part[b];
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[s]);
+  }
+
+  named_bar_sync(1, kConsumers);
+  T* y = static_cast<T*>(a.y);
+  const T* res = static_cast<const T*>(a.residual);
+  for (int idx = tid; idx < nrows * NB; idx += kConsumers) {
+    const int b = idx / nrows, r = idx - b * nrows;
+    if (b >= a.batch) break;
+    float v;
+    if constexpr (MODE == MODE_SWIGLU) {
+      const float sc = (gam != nullptr) ? sm.inv_rms[b] : 1.f;
+      const float gt = sm.acc[(size_t)(2 * r) * NB + b] * sc;
+      const float up = sm.acc[(size_t)(2 * r + 1) * NB + b] * sc;
+      v = silu(gt) * up;
+    } else if constexpr (MODE == MODE_NORM) {
+      v = sm.acc[(size_t)r * NB + b] * sm.inv_rms[b];
+    } else {
+      v = sm.acc[(size_t)r * NB + b];
+    }
+    const size_t o = (size_t)b * a.d_out + row0 + r;
+    if (res != nullptr) v += Elem<T>::to_f(res[o]);
+    y[o] = Elem<T>::from_f(v);
+  }
+}
+
+template <typename T, int NB, int MODE>
+int launch_nb(GemvArgs a, cudaStream_t st, const DeviceInfo& dev) {
+  constexpr int KCG = (NB >= 8) ? 1 : 8 / NB;    // x registers: NB * KCG * 8 = 64
+  constexpr int NMAT = (MODE == MODE_SWIGLU) ? 2 : 1;
+  a.kc = 256 * KCG;
+  a.nchunks = (a.d_in + a.kc - 1) / a.kc;
+  const int seg_max = a.kc < a.d_in ? a.kc : a.d_in;
+  const int slot_bytes = a.kc * (int)sizeof(T);
+  a.slots = kStageBytes / slot_bytes;            // 8 .. 64, multiple of 8
+  (void)seg_max;
+  const int grid = a.d_out < dev.num_sms ? a.d_out : dev.num_sms;
+  a.max_rows = (a.d_out + grid - 1) / grid;
+  size_t fixed = (size_t)a.max_rows * NMAT * NB * sizeof(float) + NB * sizeof(float) + 64;
+  int nst = kMaxStages;
+  while (nst > 2 && (size_t)nst * (kStageBytes + 16) + fixed > (size_t)dev.max_smem_optin) --nst;
+  a.nstages = nst;
+  const size_t smem = (size_t)nst * (kStageBytes + 16) + fixed;
+  if (smem > (size_t)dev.max_smem_optin) return DBK_ESHAPE;
+
+  auto kern = gemv_stream_kernel<T, NB, MODE, KCG>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return (int)e;
+  return launch_pdl(reinterpret_cast<const void*>(kern), dim3(grid), dim3(kThreads), smem, st, &a);
+}
+
+template <typename T, int MODE>
+int launch_t(const GemvArgs& a, cudaStream_t st, const DeviceInfo& dev) {
+  if (a.batch <= 1) return launch_nb<T, 1, MODE>(a, st, dev);
+  if (a.batch <= 2) return launch_nb<T, 2, MODE>(a, st, dev);
+  if (a.batch <= 4) return launch_nb<T, 4, MODE>(a, st, dev);
+  return launch_nb<T, 8, MODE>(a, st, dev);
+}
+
+int gemv_dispatch(int mode, GemvArgs a, int dtype, cudaStream_t st) {
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc) return rc;
+  if (dtype == DBK_F16) {
+    switch (mode) {
+      case MODE_PLAIN: return launch_t<__half, MODE_PLAIN>(a, st, dev);
+      case MODE_NORM: return launch_t<__half, MODE_NORM>(a, st, dev);
+      default: return launch_t<__half, MODE_SWIGLU>(a, st, dev);
+    }
+  }
+  switch (mode) {
+    case MODE_PLAIN: return launch_t<__nv_bfloat16, MODE_PLAIN>(a, st, dev);
+    case MODE_NORM: return launch_t<__nv_bfloat16, MODE_NORM>(a, st, dev);
+    default: return launch_t<__nv_bfloat16, MODE_SWIGLU>(a, st, dev);
+  }
+}
+
+int check_common(const void* x, const void* w, const void* y, int batch, int d_in, int d_out,
+                 int dtype) {
+  if (!x || !w || !y) return DBK_ENULL;
+  if (dtype != DBK_F16 && dtype != DBK_BF16) return DBK_EDTYPE;
+  if (batch < 1 || d_in < 8 || d_out < 1 || (d_in % 8) != 0) return DBK_ESHAPE;
+  if (!aligned16(x) || !aligned16(w)) return DBK_EALIGN;
+  return DBK_OK;
+}
+
+}  // namespace
+}  // namespace dbk
+
+using namespace dbk;
+
+extern "C" int dbk_rmsnorm_gemv(const void* x, const void* gamma, const void* W, void* y,
+                                int batch, int d_in, int d_out, float eps, int dtype,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_common(x, W, y, batch, d_in, d_out, dtype);
+  if (rc) return rc;
+  if (!gamma) return DBK_ENULL;
+  if (!aligned16(gamma)) return DBK_EALIGN;
+  if (batch > kSimtMaxBatch)
+    return dbk_tc_rmsnorm_gemv(x, gamma, W, y, batch, d_in, d_out, eps, dtype, workspace,
+                               workspace_bytes, stream);
+  GemvArgs a{};
+  a.x = x; a.gamma = gamma; a.w0 = W; a.y = y;
+  a.batch = batch; a.d_in = d_in; a.d_out = d_out; a.eps = eps;
+  return gemv_dispatch(MODE_NORM, a, dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dbk_gateup_swiglu(const void* x, const void* gamma, const void* Wg,
+                                 const void* Wu, void* h, int batch, int d_in, int d_ff,
+                                 float eps, int dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  int rc = check_common(x, Wg, h, batch, d_in, d_ff, dtype);
+  if (rc) return rc;
+  if (!Wu) return DBK_ENULL;
+  if (!aligned16(Wu) || (gamma && !aligned16(gamma))) return DBK_EALIGN;
+  if (batch > kSimtMaxBatch)
+    return dbk_tc_gateup_swiglu(x, gamma, Wg, Wu, h, batch, d_in, d_ff, eps, dtype, workspace,
+                                workspace_bytes, stream);
+  GemvArgs a{};
+  a.x = x; a.gamma = gamma; a.w0 = Wg; a.w1 = Wu; a.y = h;
+  a.batch = batch; a.d_in = d_in; a.d_out = d_ff; a.eps = eps;
+  return gemv_dispatch(MODE_SWIGLU, a, dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dbk_gemv(const void* x, const void* W, const void* residual, void* y, int batch,
+                        int d_in, int d_out, int dtype, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  int rc = check_common(x, W, y, batch, d_in, d_out, dtype);
+  if (rc) return rc;
+  if (batch > kSimtMaxBatch)
+    return dbk_tc_gemv(x, W, residual, y, batch, d_in, d_out, dtype, workspace,
+                       workspace_bytes, stream);
+  GemvArgs a{};
+  a.x = x; a.w0 = W; a.residual = residual; a.y = y;
+  a.batch = batch; a.d_in = d_in; a.d_out = d_out;
+  return gemv_dispatch(MODE_PLAIN, a, dtype, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,211 @@
+"""PyTorch-facing fused decode operations (the drop-in fused stages).
+
+Each function validates tensors, allocates the output (and, once per shape, a
+zero-filled workspace), and calls the C ABI on the current CUDA stream. No
+host synchronisation happens, so every op can be captured in a CUDA graph and
+used as a ``Sequence`` stage or as ``Sequence.profile(fused=...)``.
+
+There is deliberately no CPU path: a tensor that is not on a CUDA device, or a
+missing kernel library, raises.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from . import _native as N
+
+_DTYPES = {torch.float16: N.DBK_F16, torch.bfloat16: N.DBK_BF16}
+_ws_lock = threading.Lock()
+_ws_cache: dict[tuple, torch.Tensor] = {}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"decodebench_b200 kernels take float16 or bfloat16, got {t.dtype}")
+
+
+def _need_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("decodebench_b200 ops run on CUDA tensors only (no CPU fallback)")
+        if not t.is_contiguous():
+            raise ValueError("decodebench_b200 ops need contiguous tensors")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    return dev
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def workspace_bytes_flashdecode(batch: int, n_q_heads: int, n_kv_heads: int, max_len: int,
+                                split_tokens: int = 0) -> int:
+    return N.load().dbk_flashdecode_workspace_bytes(batch, n_q_heads, n_kv_heads, max_len,
+                                                    split_tokens)
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _workspace(key: tuple, nbytes: int, device: torch.device,
+              given: torch.Tensor | None = None) -> torch.Tensor | None:
+    """Zero-filled workspace for one call.
+
+    ``given`` (a caller-owned uint8 CUDA tensor, zero-filled before its first
+    use) wins; otherwise one cached workspace per (device, op shape) is reused:
+    every kernel leaves its workspace zero-filled again, so calls ordered on one
+    stream (or replayed from one graph) may share it. Calls that can run
+    concurrently on different streams must each pass their own ``workspace=``.
+    """
+    if nbytes == 0:
+        return None
+    if given is not None:
+        if given.dtype != torch.uint8 or not given.is_cuda or given.numel() < nbytes:
+            raise ValueError(f"workspace must be a uint8 CUDA tensor of >= {nbytes} bytes")
+        return given
+    full_key = (device.index,) + key
+    with _ws_lock:
+        ws = _ws_cache.get(full_key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+            _ws_cache[full_key] = ws
+        return ws
+
+
+def rmsnorm_gemv(x: torch.Tensor, gamma: torch.Tensor, W: torch.Tensor, eps: float = 1e-6,
+                 out: torch.Tensor | None = None,
+                 workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """F1: ``linear(rmsnorm(x) * gamma, W)`` for x [batch, d_in], W [d_out, d_in]."""
+    dev = _need_cuda(x, gamma, W, out)
+    dt = _dtype_code(x)
+    if gamma.dtype != x.dtype or W.dtype != x.dtype:
+        raise TypeError("x, gamma and W must share one dtype")
+    x2 = x.reshape(-1, x.shape[-1])
+    batch, d_in = x2.shape
+    d_out = W.shape[0]
+    if W.shape != (d_out, d_in) or gamma.numel() != d_in:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)}, gamma {tuple(gamma.shape)}, "
+                         f"W {tuple(W.shape)}")
+    y = out if out is not None else torch.empty(*x.shape[:-1], d_out, dtype=x.dtype, device=dev)
+    nb = N.load().dbk_workspace_bytes(N.DBK_OP_RMSNORM_GEMV, batch, d_in, d_out)
+    ws = _workspace(("f1", batch, d_in, d_out), nb, dev, workspace)
+    N.check("dbk_rmsnorm_gemv", N.load().dbk_rmsnorm_gemv(
+        x2.data_ptr(), gamma.data_ptr(), W.data_ptr(), y.data_ptr(), batch, d_in, d_out,
+        float(eps), dt, _ptr(ws), nb, _stream(dev)))
+    return y
+
+
+def gateup_swiglu(x: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
+                  gamma: torch.Tensor | None = None, eps: float = 1e-6,
+                  out: torch.Tensor | None = None,
+                  workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """F2: ``silu(x Wg^T) * (x Wu^T)``; with ``gamma``, x is RMS-normalised first."""
+    dev = _need_cuda(x, Wg, Wu, gamma, out)
+    dt = _dtype_code(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    batch, d_in = x2.shape
+    d_ff = Wg.shape[0]
+    if Wg.shape != (d_ff, d_in) or Wu.shape != (d_ff, d_in):
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)}, Wg {tuple(Wg.shape)}, "
+                         f"Wu {tuple(Wu.shape)}")
+    if Wg.dtype != x.dtype or Wu.dtype != x.dtype or (gamma is not None and gamma.dtype != x.dtype):
+        raise TypeError("all operands must share one dtype")
+    h = out if out is not None else torch.empty(*x.shape[:-1], d_ff, dtype=x.dtype, device=dev)
+    nb = N.load().dbk_workspace_bytes(N.DBK_OP_GATEUP_SWIGLU, batch, d_in, d_ff)
+    ws = _workspace(("f2", batch, d_in, d_ff), nb, dev, workspace)
+    N.check("dbk_gateup_swiglu", N.load().dbk_gateup_swiglu(
+        x2.data_ptr(), _ptr(gamma), Wg.data_ptr(), Wu.data_ptr(), h.data_ptr(), batch, d_in,
+        d_ff, float(eps), dt, _ptr(ws), nb, _stream(dev)))
+    return h
+
+
+def gemv(x: torch.Tensor, W: torch.Tensor, residual: torch.Tensor | None = None,
+         out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """``linear(x, W) (+ residual)`` for x [batch, d_in], W [d_out, d_in]."""
+    dev = _need_cuda(x, W, residual, out)
+    dt = _dtype_code(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    batch, d_in = x2.shape
+    d_out = W.shape[0]
+    if W.shape != (d_out, d_in):
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)}, W {tuple(W.shape)}")
+    if residual is not None and residual.numel() != batch * d_out:
+        raise ValueError("residual must have the output's shape")
+    y = out if out is not None else torch.empty(*x.shape[:-1], d_out, dtype=x.dtype, device=dev)
+    nb = N.load().dbk_workspace_bytes(N.DBK_OP_GEMV, batch, d_in, d_out)
+    ws = _workspace(("gemv", batch, d_in, d_out), nb, dev, workspace)
+    N.check("dbk_gemv", N.load().dbk_gemv(
+        x2.data_ptr(), W.data_ptr(), _ptr(residual), y.data_ptr(), batch, d_in, d_out, dt,
+        _ptr(ws), nb, _stream(dev)))
+    return y
+
+
+def mlp(x: torch.Tensor, gamma: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
+        Wd: torch.Tensor, eps: float = 1e-5, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode MLP block: down(silu(gate(rmsnorm(x))) * up(rmsnorm(x))) (+ residual)."""
+    h = gateup_swiglu(x, Wg, Wu, gamma=gamma, eps=eps)
+    return gemv(h, Wd, residual=residual)
+
+
+def flashdecode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                seq_lens: torch.Tensor | None = None, page_table: torch.Tensor | None = None,
+                scale: float | None = None, split_tokens: int = 0,
+                out: torch.Tensor | None = None,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """F4 split-KV FlashDecode for one query token per sequence.
+
+    q [batch, Hq, 128]. Contiguous caches: k/v [batch, Hkv, max_len, 128].
+    Paged caches (``page_table`` int32 [batch, max_pages]): k/v [pages, Hkv, page_size, 128].
+    ``seq_lens`` int32 [batch] (device) or None for full length. ``scale``
+    defaults to 1/sqrt(128).
+    """
+    dev = _need_cuda(q, k_cache, v_cache, seq_lens, page_table, out)
+    dt = _dtype_code(q)
+    if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise TypeError("q, k_cache and v_cache must share one dtype")
+    if k_cache.shape != v_cache.shape:
+        raise ValueError("k_cache and v_cache must have the same shape")
+    q3 = q.reshape(q.shape[0], -1, q.shape[-1])
+    batch, hq, d = q3.shape
+    if page_table is None:
+        if k_cache.dim() != 4 or k_cache.shape[0] != batch:
+            raise ValueError("contiguous cache must be [batch, Hkv, max_len, head_dim]")
+        _, hkv, max_len, _ = k_cache.shape
+        page_size, max_pages = 0, 0
+    else:
+        if page_table.dtype != torch.int32 or page_table.dim() != 2 or page_table.shape[0] != batch:
+            raise ValueError("page_table must be int32 [batch, max_pages]")
+        _, hkv, page_size, _ = k_cache.shape
+        max_pages = page_table.shape[1]
+        max_len = page_size * max_pages
+    if seq_lens is not None and (seq_lens.dtype != torch.int32 or seq_lens.numel() != batch):
+        raise ValueError("seq_lens must be int32 [batch]")
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    o = out if out is not None else torch.empty_like(q)
+    lib = N.load()
+    nb = lib.dbk_flashdecode_workspace_bytes(batch, hq, hkv, max_len, split_tokens)
+    ws = _workspace(("f4", batch, hq, hkv, max_len, split_tokens), nb, dev, workspace)
+    N.check("dbk_flashdecode", lib.dbk_flashdecode(
+        q3.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _ptr(page_table),
+        _ptr(seq_lens), o.data_ptr(), batch, hq, hkv, d, max_len, page_size, max_pages,
+        float(scale), int(split_tokens), dt, _ptr(ws), nb, _stream(dev)))
+    return o
+
+
+def take_device_error() -> int:
+    """Error code a kernel recorded after a bounded wait gave up (0 = none); clears it."""
+    return N.load().dbk_take_device_error()

@@ -1,0 +1,122 @@
+/* dbk.h - C ABI of the decodebench_b200 fused decode kernels (sm_100a).
+ *
+ * Every entry point:
+ *   - takes device pointers, sizes and a cudaStream_t passed as void*;
+ *   - allocates nothing and never synchronises (safe inside CUDA-graph capture);
+ *     scratch space is a caller-owned workspace sized by dbk_workspace_bytes();
+ *   - returns 0 on success, a negative DBK_E* code for a rejected argument, or a
+ *     positive cudaError_t value when a CUDA call fails.
+ *
+ * The reference (animeshsri14/Decodebench) launches its kernels through one
+ * by-value struct, `KernelArgs` (validation/include/decodebench_val/kernel_args.h:24-103),
+ * with geometry chosen by its harness (validation/src/bench/bench_variant.cu:376-387,
+ * :562-575, :758-770) and host checks that exit(1) (bench_variant.cu:60-70, :324-331,
+ * :689-700). These entry points replace that struct with one call per fused
+ * operation; the checks become DBK_E* return codes.
+ */
+#ifndef DBK_H_
+#define DBK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DBK_ABI_VERSION 1
+
+/* Element type of activations, weights, caches and outputs. */
+typedef enum { DBK_F16 = 0, DBK_BF16 = 1 } dbk_dtype;
+
+/* Argument errors (negative). Positive values are cudaError_t. */
+#define DBK_OK 0
+#define DBK_ENULL (-1)        /* a required pointer is NULL                         */
+#define DBK_ESHAPE (-2)       /* a size is out of the supported range                */
+#define DBK_EALIGN (-3)       /* a pointer or row is not 16-byte aligned             */
+#define DBK_EWORKSPACE (-4)   /* workspace missing or smaller than dbk_workspace_bytes */
+#define DBK_EDTYPE (-5)       /* unknown dtype                                        */
+#define DBK_EDEVICE (-6)      /* the current device is not sm_100                     */
+
+/* Operation ids for dbk_workspace_bytes(). */
+typedef enum {
+  DBK_OP_RMSNORM_GEMV = 0,
+  DBK_OP_GATEUP_SWIGLU = 1,
+  DBK_OP_GEMV = 2
+} dbk_op;
+
+/* ABI version compiled into the library (== DBK_ABI_VERSION). */
+int dbk_abi_version(void);
+
+/* Static description of a status code. */
+const char* dbk_status_string(int status);
+
+/* First error a kernel recorded after giving up a bounded wait (0 = none), and
+ * clear it. Synchronises the current device. */
+int dbk_take_device_error(void);
+
+/* Workspace bytes a GEMV-family operation needs (0 if none):
+ *   op = DBK_OP_RMSNORM_GEMV | DBK_OP_GATEUP_SWIGLU | DBK_OP_GEMV,
+ *   sizes (batch, d_in, d_out or d_ff).
+ * A workspace must be zero-filled once before its first use (e.g. cudaMemset
+ * right after allocation); every kernel leaves it zero-filled again, so one
+ * workspace serves any number of calls ordered on one stream. */
+size_t dbk_workspace_bytes(int op, int64_t batch, int64_t d_in, int64_t d_out);
+
+/* Workspace bytes of dbk_flashdecode for the given sizes (same zero-fill rule). */
+size_t dbk_flashdecode_workspace_bytes(int batch, int n_q_heads, int n_kv_heads, int max_len,
+                                       int split_tokens);
+
+/* F1: y[b, :] = W @ (x[b, :] * rsqrt(mean(x[b, :]^2) + eps) * gamma)
+ *   x [batch, d_in], gamma [d_in], W [d_out, d_in] row-major, y [batch, d_out].
+ *   fp32 accumulation; normalisation folded into the GEMV.
+ * Replaces fused f1_kernel (validation/src/kernels/fused/f1.cu:18-84, launched at
+ * bench_variant.cu:379-387) and the Python stages rmsnorm + gemv
+ * (src/decodebench/demos/llama_decode.py:36-43).
+ * batch 1..8 on CUDA cores; batch 9..256 on tcgen05 tensor cores (needs workspace). */
+int dbk_rmsnorm_gemv(const void* x, const void* gamma, const void* W, void* y,
+                     int batch, int d_in, int d_out, float eps, int dtype,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* F2: h[b, j] = silu(x[b, :] . Wg[j, :]) * (x[b, :] . Wu[j, :])
+ *   optionally with an RMSNorm prologue on x when gamma != NULL.
+ *   x [batch, d_in], Wg, Wu [d_ff, d_in], h [batch, d_ff].
+ * Replaces fused f2_kernel (validation/src/kernels/fused/f2.cu:17-76, launched at
+ * bench_variant.cu:562-575) and the Python stages gate, up, swiglu
+ * (src/decodebench/demos/llama_decode.py:77-87). */
+int dbk_gateup_swiglu(const void* x, const void* gamma, const void* Wg, const void* Wu,
+                      void* h, int batch, int d_in, int d_ff, float eps, int dtype,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Plain GEMV / thin GEMM: y[b, :] = W @ x[b, :] (+ residual[b, :] when not NULL).
+ * Replaces the unfused gemv_kernel role (validation/src/kernels/unfused/gemv.cu:15-48)
+ * and F.linear (llama_decode.py:41-43); used for the MLP down projection. */
+int dbk_gemv(const void* x, const void* W, const void* residual, void* y,
+             int batch, int d_in, int d_out, int dtype,
+             void* workspace, size_t workspace_bytes, void* stream);
+
+/* F4: split-KV FlashDecode, one query token per sequence.
+ *   q   [batch, n_q_heads, head_dim]
+ *   out [batch, n_q_heads, head_dim]
+ *   Contiguous cache (page_table == NULL):
+ *       k_cache, v_cache [batch, n_kv_heads, max_len, head_dim]
+ *   Paged cache (page_table != NULL, int32 [batch, max_pages_per_seq]):
+ *       k_cache, v_cache [num_pages, n_kv_heads, page_size, head_dim]
+ *   seq_lens: int32 [batch] on the device, or NULL (every sequence has max_len).
+ *   q head h reads kv head h / (n_q_heads / n_kv_heads) (GQA; MHA when equal).
+ *   scale multiplies q.k (1/sqrt(head_dim) for standard attention).
+ *   split_tokens: tokens per split-KV work item (multiple of 64), 0 = automatic.
+ * Replaces f4_partial_kernel + f4_reduce_kernel (validation/src/kernels/fused/f4.cu:173-319,
+ * launched at bench_variant.cu:758-763) and the Python stages scores, softmax,
+ * weighted_v (llama_decode.py:120-134). head_dim 128 only. */
+int dbk_flashdecode(const void* q, const void* k_cache, const void* v_cache,
+                    const int32_t* page_table, const int32_t* seq_lens, void* out,
+                    int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len,
+                    int page_size, int max_pages_per_seq, float scale, int split_tokens,
+                    int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DBK_H_ */

@@ -1,0 +1,32 @@
+"""Shared pytest configuration: the `gpu` marker, auto-skipped without CUDA."""
+
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: tests that need a B200 (sm_100a) GPU")
+
+
+def _has_cuda() -> bool:
+    try:
+        import torch
+
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+def pytest_collection_modifyitems(config, items):
+    if _has_cuda():
+        return
+    skip = pytest.mark.skip(reason="CUDA not available")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
