@@ -36,6 +36,7 @@ constexpr int kConsumers = kWarps * 32;
 constexpr int kThreads = kConsumers + 32;
 constexpr int kMaxStages = 6;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMrg = kD + 4;             // merge-row stride: o[128], m, l, pad (16-byte rows)
 
 struct FdArgs {
   const void* q;          // [batch, Hq, 128]
@@ -117,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const FdArgs a
   constexpr int kStage = 2 * kTile * kD * (int)sizeof(T);       // K tile | V tile
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.nstages * kStage);
   uint64_t* empty = full + a.nstages;
-  float* mrg = reinterpret_cast<float*>(empty + a.nstages);     // [kWarps][G][kD + 2] (o, m, l)
+  float* mrg = reinterpret_cast<float*>(empty + a.nstages);     // [kWarps][G][kMrg] (o, m, l)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -267,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const FdArgs a
     named_bar_sync(1, kConsumers);   // previous item's readers of mrg are done
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float* dst = mrg + (warp * G + g) * (kD + 2);
+      float* dst = mrg + (warp * G + g) * kMrg;
       *reinterpret_cast<float4*>(dst + 4 * lane) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
       if (lane == 0) { dst[kD] = m[g]; dst[kD + 1] = l[g]; }
     }
@@ -278,11 +279,11 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const FdArgs a
       const int g = idx / kD, d = idx - g * kD;
       float M = -INFINITY;
 #pragma unroll
-      for (int ww = 0; ww < kWarps; ++ww) M = fmaxf(M, mrg[(ww * G + g) * (kD + 2) + kD]);
+      for (int ww = 0; ww < kWarps; ++ww) M = fmaxf(M, mrg[(ww * G + g) * kMrg + kD]);
       float L = 0.f, O = 0.f;
 #pragma unroll
       for (int ww = 0; ww < kWarps; ++ww) {
-        const float* src = mrg + (ww * G + g) * (kD + 2);
+        const float* src = mrg + (ww * G + g) * kMrg;
         const float f = exp2f(src[kD] - M);   // warps without tokens: m = -inf -> 0
         L = fmaf(f, src[kD + 1], L);
         O = fmaf(f, src[d], O);
@@ -359,7 +360,7 @@ size_t ws_bytes_for(const FdPlan& p, int batch, int hq, int hkv) {
 template <typename T, int G>
 int launch_g(FdArgs a, cudaStream_t st, const DeviceInfo& dev, int grid) {
   constexpr int kStage = 2 * kTile * kD * (int)sizeof(T);
-  const size_t fixed = (size_t)kWarps * G * (kD + 2) * 4 + G * 8 + 64;
+  const size_t fixed = (size_t)kWarps * G * kMrg * 4 + G * 8 + 64;
   int nst = kMaxStages;
   while (nst > 2 && (size_t)nst * (kStage + 16) + fixed > (size_t)dev.max_smem_optin - 1024) --nst;
   a.nstages = nst;
