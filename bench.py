@@ -394,7 +394,109 @@ class F4(Workload):
         return self.costs.flashdecode_bytes([self.L], self.cpu_heads, self.cpu_heads)
 
 
-WORKLOADS = {"f2": F2, "f1": F1, "f4": F4}
+class GQA(F4):
+    """batch 8, 64 q heads, 8 kv heads, head_dim 128, bf16 paged
+    KV (64-token pages, random page permutation), lengths ~U[1024, 32768] seeded.
+    With N ranks the kv heads are sharded (8/N per rank with their 8 q heads)."""
+
+    name = "gqa"
+
+    def __init__(self, rank, world, torch, batch=8, hq=64, hkv=8, ps=64):
+        import numpy as np
+
+        from decodebench_b200 import costs, ops
+
+        self.t, self.ops, self.costs = torch, ops, costs
+        self.rank, self.world, self.batch = rank, world, batch
+        self.hq_total, self.hkv_total = hq, hkv
+        self.hkv, self.hq = hkv // world, hq // world
+        rng = np.random.default_rng(2024)
+        self.lens_np = rng.integers(1024, 32769, size=batch).astype(np.int32)
+        pages_per = [(int(n) + ps - 1) // ps for n in self.lens_np]
+        maxp = max(pages_per)
+        npages = sum(pages_per)
+        perm = rng.permutation(npages).astype(np.int32)
+        table = np.zeros((batch, maxp), np.int32)
+        o = 0
+        for b, n in enumerate(pages_per):
+            table[b, :n] = perm[o:o + n]
+            o += n
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(11 + rank)
+        kv_bytes = 2 * npages * self.hkv * ps * 128 * 2
+        self.nrep = max(1, min(8, math.ceil(2 * 126e6 / kv_bytes)))
+        self.KV = [(torch.randn(npages, self.hkv, ps, 128, generator=g, device=dev).bfloat16(),
+                    torch.randn(npages, self.hkv, ps, 128, generator=g, device=dev).bfloat16())
+                   for _ in range(self.nrep)]
+        self.table = torch.from_numpy(table).to(dev)
+        self.lens = torch.from_numpy(self.lens_np).to(dev)
+        self.table_bytes = table.nbytes
+        xg = torch.Generator().manual_seed(42)
+        self.q_cpu = torch.randn(batch, self.hq, 128, generator=xg).bfloat16()
+        self.q = self.q_cpu.to(dev)
+        self.o = torch.empty_like(self.q)
+        self.o_full = torch.empty(world, *self.o.shape, dtype=self.o.dtype, device=dev)
+        self.L = int(self.lens_np.max())
+        self.H = hq
+
+    def describe(self):
+        return {"workload": "GQA paged FlashDecode, batch 8, 64 q / 8 kv heads, head_dim 128, "
+                            "bf16, 64-token pages, lengths ~U[1024,32768] (BASELINE config 5)",
+                "global_batch": self.batch, "seq_lens": [int(x) for x in self.lens_np],
+                "parallelism": ("single GPU" if self.world == 1 else
+                                f"kv heads sharded {self.hkv}/rank, NCCL all-gather of out"),
+                "kv_replicas": self.nrep, "l2": f"paged K/V {self.nrep} replica(s), "
+                f"{sum(t.nbytes for kv in self.KV for t in kv) / 1e6:.0f} MB > 126 MB L2"}
+
+    def step_bytes_total(self):
+        return self.costs.flashdecode_bytes(self.lens_np, self.hq_total, self.hkv_total,
+                                            page_table_bytes=self.table_bytes)
+
+    def launch_bytes(self):
+        return self.costs.flashdecode_bytes(self.lens_np, self.hq, self.hkv,
+                                            page_table_bytes=self.table_bytes)
+
+    def run_kernel(self, rep):
+        K, V = self.KV[rep % self.nrep]
+        self.ops.flashdecode(self.q, K, V, seq_lens=self.lens, page_table=self.table, out=self.o)
+
+    def e2e_setup(self):
+        t = self.t
+        self.q_host = self.q_cpu.pin_memory()
+        self.out_host = t.empty(self.world * self.o.numel(), dtype=t.bfloat16).pin_memory()
+        self.q_dev = t.empty_like(self.q)
+        self._e2e_i = 0
+        return self.q_host.nbytes, self.out_host.nbytes
+
+    def e2e_step(self):
+        K, V = self.KV[self._e2e_i % self.nrep]
+        self._e2e_i += 1
+        self.q_dev.copy_(self.q_host, non_blocking=True)
+        o = self.ops.flashdecode(self.q_dev, K, V, seq_lens=self.lens, page_table=self.table)
+        if self.world > 1:
+            full = self.t.empty(self.world, *o.shape, dtype=o.dtype, device=o.device)
+            self.t.distributed.all_gather_into_tensor(full, o)
+            o = full
+        self.out_host.copy_(o.reshape(-1), non_blocking=True)
+
+    def cpu_setup(self, frac_rows: float = 1.0):
+        import numpy as np
+
+        rng = np.random.default_rng(5)
+        L = max(64, int(int(self.lens_np[0]) * frac_rows))
+        self.cpu_len = L
+        # one sequence, one kv head with its 8 q heads, through the reference's attention_ref
+        self.cq = rng.standard_normal((8, 128), dtype=np.float32) / math.sqrt(128)
+        K = rng.standard_normal((L, 128), dtype=np.float32)
+        V = rng.standard_normal((L, 128), dtype=np.float32)
+        self.cK = np.broadcast_to(K, (8, L, 128)).copy()
+        self.cV = np.broadcast_to(V, (8, L, 128)).copy()
+
+    def cpu_step_bytes(self):
+        return self.costs.flashdecode_bytes([self.cpu_len], 8, 1)
+
+
+WORKLOADS = {"f2": F2, "f1": F1, "f4": F4, "gqa": GQA}
 
 
 # ---------------------------------------------------------------- timing
@@ -413,42 +515,66 @@ def barrier_sync(torch):
         torch.cuda.synchronize()
 
 
-def capture_steps(torch, wl: Workload, with_exchange: bool):
-    """One CUDA graph per weight replica: kernel (+ exchange)."""
-    graphs = []
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        for r in range(wl.nrep):
+def _capture(torch, body):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        body()
+    return g
+
+
+class StepGraphs:
+    """CUDA graphs of the step: one graph of `per` consecutive steps (rotating
+    the weight replicas; consecutive kernels overlap prologue and tail through
+    programmatic dependent launch) plus one single-step graph per replica, so
+    that exactly K steps can be replayed."""
+
+    def __init__(self, torch, wl, with_exchange: bool, per: int = 32):
+        self.torch = torch
+
+        def one(r):
             wl.run_kernel(r)
             if with_exchange:
                 wl.exchange()
-    torch.cuda.current_stream().wait_stream(s)
-    torch.cuda.synchronize()
-    for r in range(wl.nrep):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            wl.run_kernel(r)
-            if with_exchange:
-                wl.exchange()
-        graphs.append(g)
-    torch.cuda.synchronize()
-    return graphs
+
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):          # warm-up outside capture (workspaces, attributes)
+            for r in range(wl.nrep):
+                one(r)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.per = max(wl.nrep, (per // wl.nrep) * wl.nrep)
+        self.big = _capture(torch, lambda: [one(r % wl.nrep) for r in range(self.per)])
+        self.small = [_capture(torch, lambda r=r: one(r)) for r in range(wl.nrep)]
+        torch.cuda.synchronize()
+
+    def run(self, steps: int) -> None:
+        for _ in range(steps // self.per):
+            self.big.replay()
+        for i in range(steps % self.per):
+            self.small[i % len(self.small)].replay()
 
 
-def timed(torch, fn, steps: int, warmup: int) -> float:
-    """Device ms for `steps` calls of fn(i), barrier + sync on both sides, max over ranks."""
-    for i in range(warmup):
-        fn(i)
+def timed(torch, run, steps: int, warmup: int) -> float:
+    """Device ms for run(steps) after run(warmup); barrier + sync on both sides,
+    CUDA events on the current stream, max over ranks."""
+    if warmup:
+        run(warmup)
     barrier_sync(torch)
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     a.record()
-    for i in range(steps):
-        fn(warmup + i)
+    run(steps)
     b.record()
     barrier_sync(torch)
     return dist_max(torch, a.elapsed_time(b))
+
+
+def loop(fn):
+    def run(n):
+        for _ in range(n):
+            fn()
+    return run
 
 
 def cpu_time(wl, threads: int, budget_s: float, steps: int | None = None, warmup: int = 1):
@@ -546,22 +672,20 @@ def main() -> int:
     wl = WORKLOADS[args.workload](rank, world, torch)
 
     # --- device-timed value: graphs of kernel + exchange, rotated over replicas
-    graphs = capture_steps(torch, wl, with_exchange=True)
+    graphs = StepGraphs(torch, wl, with_exchange=True)
     sampler = ClockSampler(dev_index)
     sampler.start()
-    for i in range(args.warmup):
-        graphs[i % len(graphs)].replay()
+    graphs.run(args.warmup)
     barrier_sync(torch)
     t_begin = time.perf_counter()
-    ms = timed(torch, lambda i: graphs[i % len(graphs)].replay(), args.steps, 0)
+    ms = timed(torch, graphs.run, args.steps, 0)
     t_end = time.perf_counter()
     # Keep identical steps running until the sampler has seen >= 5 samples, so
     # that a short timed region still has a clock record around it.
     pad_until = time.perf_counter() + 2.0
     while sampler.ok and sampler.count_between(t_begin, time.perf_counter()) < 5 \
             and time.perf_counter() < pad_until:
-        for i in range(64):
-            graphs[i % len(graphs)].replay()
+        graphs.run(256)
         torch.cuda.synchronize()
     clocks = sampler.summary(t_begin, max(t_end, time.perf_counter()))
     sampler.stop()
@@ -570,8 +694,8 @@ def main() -> int:
 
     # --- kernel-only timing for the roofline (the dominant, and only, kernel)
     if world > 1:
-        kgraphs = capture_steps(torch, wl, with_exchange=False)
-        kms = timed(torch, lambda i: kgraphs[i % len(kgraphs)].replay(), args.steps, args.warmup)
+        kgraphs = StepGraphs(torch, wl, with_exchange=False)
+        kms = timed(torch, kgraphs.run, args.steps, args.warmup)
     else:
         kms = ms
     k_us = kms * 1e3 / args.steps
@@ -586,7 +710,7 @@ def main() -> int:
 
     # --- e2e through the public API with host buffers
     h2d, d2h = wl.e2e_setup()
-    e_ms = timed(torch, lambda i: wl.e2e_step(), args.steps, args.warmup)
+    e_ms = timed(torch, loop(wl.e2e_step), args.steps, args.warmup)
     e_us = e_ms * 1e3 / args.steps
     e2e = {"value": round(wl.step_bytes_total() / (e_us * 1e-6) / 1e9, 1), "unit": "GB/s",
            "us_per_step": round(e_us, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -1,6 +1,7 @@
 // dbk_internal.h - host-side helpers shared by the C-ABI translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -23,6 +24,14 @@ struct DeviceInfo {
 int current_device_info(DeviceInfo* out);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Encode a 2-D tiled TMA descriptor over a row-major [rows, inner] matrix of
+// 16-bit elements (dtype DBK_F16 / DBK_BF16), box [box_rows, box_inner], with
+// 128-byte swizzle when swizzle128 (box_inner * 2 must then be 128), zero
+// fill out of bounds. Returns DBK_OK or a DBK_E* / cudaError_t code.
+int encode_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t inner, uint64_t rows,
+                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                   bool swizzle128);
 
 // Launch `func(*args)` (one by-value struct parameter) with programmatic
 // dependent launch enabled unless DBK_PDL=0 is set in the environment.

@@ -9,20 +9,25 @@
 // m* = max m_s, o = sum e^(m_s-m*) o_s / sum e^(m_s-m*) l_s  (f4.cu:294-319).
 //
 // Design (B200):
-//   * work items are (b, hk, split) with split_tokens tokens each; CTAs (one per
-//     SM, persistent) take items round-robin, so a ragged batch still spreads
-//     over all 148 SMs;
-//   * a producer warp streams each item's K and V in 64-token tiles with
-//     cp.async.bulk into a ring of 32 KB stages (K tile | V tile); a paged cache
-//     ([page, kv_head, page_size, 128], the per-head page block contiguous) is
-//     gathered page-run by page-run through the int32 page table;
-//   * eight consumer warps each take 8 tokens of a tile and keep their own
-//     online-softmax state (m, l, o) for the G query heads: no block barrier per
-//     tile; lane l owns head dims 4l..4l+3 of q and o;
-//   * at the end of an item the warps' states are merged in shared memory; a
-//     single-split sequence writes its output directly, otherwise the partial
-//     goes to the workspace and the last CTA to finish a (b, hk) (atomic
-//     counter, self-resetting) performs the LSE merge: no second launch.
+//   * Schedule: the (b, kv head) rows of 64-token tiles are laid end to end and
+//     CTA c (one per SM, persistent) takes tiles [c*T/grid, (c+1)*T/grid): every
+//     SM gets the same number of tiles (within one) whatever the sequence
+//     lengths, and a CTA's range cuts at most two rows, so it emits at most two
+//     partials. A row covered by one CTA is written directly; otherwise the last
+//     CTA to finish a row (self-resetting atomic counter) merges its partials.
+//   * A producer warp streams K and V tiles into a ring of 32 KB stages tracked
+//     by mbarriers, gathering a paged cache ([page, kv_head, page_size, 128],
+//     per-head page blocks contiguous) through the int32 page table.
+//   * G <= 2 (MHA-like): cp.async.bulk row runs; eight consumer warps each take
+//     8 tokens of a tile with their own online-softmax state on CUDA cores.
+//   * G >= 4 (GQA): the G query heads of a kv head form the M=16 rows of
+//     mma.m16n8k16 tiles. K/V arrive by tiled TMA (cp.async.bulk.tensor) with a
+//     128-byte swizzle so ldmatrix reads are conflict free; two groups of four
+//     warps take alternate stages, each warp 16 tokens: S = Q K^T (fp32
+//     accumulate), online softmax in registers, O += P V with P split into a
+//     high and a low 16-bit part so the probabilities keep fp32-like accuracy.
+#include <type_traits>
+
 #include "common.cuh"
 #include "dbk_internal.h"
 
@@ -35,127 +40,185 @@ constexpr int kWarps = 8;
 constexpr int kConsumers = kWarps * 32;
 constexpr int kThreads = kConsumers + 32;
 constexpr int kMaxStages = 6;
+constexpr int kBoxRows = 16;            // TMA box height (tokens) on the tensor-core path
+constexpr int kMaxBatchSmem = 1024;     // sequences whose tile offsets live in shared memory
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kMrg = kD + 4;             // merge-row stride: o[128], m, l, pad (16-byte rows)
+constexpr int kMrg = kD + 4;            // merge-row stride: o[128], m, l, pad (16-byte rows)
 
 struct FdArgs {
+  CUtensorMap kmap;       // tensor-core path: 2-D view [rows, 128] of the K cache
+  CUtensorMap vmap;
   const void* q;          // [batch, Hq, 128]
   const void* k;          // contiguous [batch, Hkv, max_len, 128] | paged [pages, Hkv, ps, 128]
   const void* v;
   const int32_t* pages;   // [batch, max_pages] or nullptr
   const int32_t* lens;    // [batch] or nullptr
   void* out;              // [batch, Hq, 128]
-  float* part_o;          // [items_cap, G, 128]
-  float2* part_ml;        // [items_cap, G]
+  float* part_o;          // [2 * grid, G, 128]
+  float2* part_ml;        // [2 * grid, G]
   int* done;              // [batch * Hkv] arrival counters (zero between launches)
   int batch, hq, hkv, max_len, page_size, max_pages;
-  int split_tokens;       // multiple of kTile
-  int items_per_seqhead;  // ceil(max_len / split_tokens): item-id stride
   float qscale;           // scale * log2(e)
   int nstages;
-};
-
-struct Item {
-  int b, hk, s, t0, ntok, nsplit;
 };
 
 __device__ __forceinline__ int seq_len(const FdArgs& a, int b) {
   return a.lens ? min(max(a.lens[b], 0), a.max_len) : a.max_len;
 }
 
-// Item enumeration: id -> (b, hk, split), skipping splits past len_b.
-// Items are numbered densely over (b, hk, s < nsplit_b) in that order; every CTA
-// walks the same enumeration, so producer and consumers agree without messages.
-struct ItemWalker {
+// Tile offsets: tile0[b] = first global tile of (b, kv head 0); row (b, hk)
+// starts at tile0[b] + hk * ntiles(b). Computed by warp 0 with a warp scan.
+__device__ void build_tile_offsets(const FdArgs& a, int* tile0, int lane) {
+  int carry = 0;
+  for (int base = 0; base < a.batch; base += 32) {
+    const int b = base + lane;
+    const int nt = (b < a.batch) ? ((seq_len(a, b) + kTile - 1) / kTile) * a.hkv : 0;
+    int incl = nt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (b < a.batch) tile0[b] = carry + incl - nt;
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) tile0[a.batch] = carry;
+}
+
+// Walks the global tile sequence: current (b, hk, tile within row).
+struct TileWalker {
   const FdArgs& a;
-  int b = 0, hk = 0, s = 0, nsplit = 0;
-  __device__ explicit ItemWalker(const FdArgs& args) : a(args) { reset_seq(); }
-  __device__ void reset_seq() {
-    while (b < a.batch) {
-      const int L = seq_len(a, b);
-      nsplit = (L + a.split_tokens - 1) / a.split_tokens;
-      if (nsplit > 0) return;
-      ++b;
+  const int* tile0;
+  int b, hk, tt, ntb, len;   // ntb = tiles per row of sequence b
+  __device__ TileWalker(const FdArgs& args, const int* t0, int u) : a(args), tile0(t0) {
+    int lo = 0, hi = a.batch - 1;             // last b with tile0[b] <= u
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tile0[mid] <= u) lo = mid; else hi = mid - 1;
     }
+    b = lo;
+    len = seq_len(a, b);
+    ntb = (len + kTile - 1) / kTile;
+    while (ntb == 0) { ++b; len = seq_len(a, b); ntb = (len + kTile - 1) / kTile; }
+    const int off = u - tile0[b];
+    hk = off / ntb;
+    tt = off - hk * ntb;
   }
-  __device__ bool valid() const { return b < a.batch; }
-  __device__ void advance(int n) {  // move forward n items
-    while (n > 0 && valid()) {
-      const int left = nsplit - s;
-      if (n < left) { s += n; return; }
-      n -= left;
-      s = 0;
-      if (++hk == a.hkv) { hk = 0; ++b; reset_seq(); }
-    }
+  __device__ void next() {
+    if (++tt < ntb) return;
+    tt = 0;
+    if (++hk < a.hkv) return;
+    hk = 0;
+    do { ++b; if (b >= a.batch) return; len = seq_len(a, b); ntb = (len + kTile - 1) / kTile; }
+    while (ntb == 0);
   }
-  __device__ Item get() const {
-    Item it;
-    it.b = b; it.hk = hk; it.s = s; it.nsplit = nsplit;
-    it.t0 = s * a.split_tokens;
-    it.ntok = min(a.split_tokens, seq_len(a, b) - it.t0);
-    return it;
-  }
+  __device__ int row() const { return b * a.hkv + hk; }
+  __device__ int row_start() const { return tile0[b] + hk * ntb; }
+  __device__ int ntok() const { return min(kTile, len - tt * kTile); }
 };
 
-// Address of K/V row (token t of (b, hk)); paged caches go through the table.
-template <typename T>
-__device__ __forceinline__ const T* kv_row(const FdArgs& a, const void* base, int b, int hk,
-                                           int t, int* run) {
-  const T* p = static_cast<const T*>(base);
+// Row index (into the 2-D cache view) of token t of (b, hk), and tokens left
+// in its page run.
+__device__ __forceinline__ int64_t kv_rowidx(const FdArgs& a, int b, int hk, int t, int* run) {
   if (a.pages == nullptr) {
     *run = 1 << 30;
-    return p + (((size_t)b * a.hkv + hk) * a.max_len + t) * kD;
+    return ((int64_t)b * a.hkv + hk) * a.max_len + t;
   }
   const int pg = a.pages[(size_t)b * a.max_pages + t / a.page_size];
   const int off = t % a.page_size;
-  *run = a.page_size - off;   // tokens left in this page
-  return p + (((size_t)pg * a.hkv + hk) * a.page_size + off) * kD;
+  *run = a.page_size - off;
+  return ((int64_t)pg * a.hkv + hk) * a.page_size + off;
 }
 
+// CTA whose tile range contains global tile u (ranges [c*T/grid, (c+1)*T/grid)).
+__device__ __forceinline__ int owner(int64_t u, int64_t T, int64_t grid) {
+  return (int)(((u + 1) * grid + T - 1) / T - 1);
+}
+__device__ __forceinline__ int range_start(int64_t c, int64_t T, int64_t grid) {
+  return (int)(c * T / grid);
+}
+
+// ------------------------------------------------------------------ kernel
 template <typename T, int G>
-__global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const FdArgs a) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  constexpr int kStage = 2 * kTile * kD * (int)sizeof(T);       // K tile | V tile
+__global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_constant__ FdArgs a) {
+  constexpr bool kMma = (G >= 4);
+  constexpr int kHalf = kTile * 64 * (int)sizeof(T);        // 64 tokens x 64 dims (8 KB)
+  constexpr int kStage = 2 * kTile * kD * (int)sizeof(T);   // K tile | V tile (32 KB)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.nstages * kStage);
   uint64_t* empty = full + a.nstages;
-  float* mrg = reinterpret_cast<float*>(empty + a.nstages);     // [kWarps][G][kMrg] (o, m, l)
+  float* mrg = reinterpret_cast<float*>(empty + a.nstages);              // [kWarps][G][kMrg]
+  int* tile0 = reinterpret_cast<int*>(mrg + kWarps * G * kMrg);           // [batch + 1]
+  __shared__ int s_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
+    // A stage is released by every consumer warp (CUDA-core path) or by the
+    // four warps of the group that consumed it (tensor-core path).
     for (int s = 0; s < a.nstages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kWarps);
+      mbar_init(&empty[s], kMma ? 4 : kWarps);
     }
     fence_barrier_init();
   }
+  if (warp == 0) build_tile_offsets(a, tile0, lane);
   __syncthreads();
   asm volatile("griddepcontrol.launch_dependents;");
+
+  // Sequences of length 0 have no tiles: their output is defined as zeros.
+  if (blockIdx.x == 0 && a.lens != nullptr && warp < kWarps) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    T* out = static_cast<T*>(a.out);
+    for (int b = 0; b < a.batch; ++b)
+      if (seq_len(a, b) == 0)
+        for (int i = tid; i < a.hq * kD; i += kConsumers)
+          out[(size_t)b * a.hq * kD + i] = Elem<T>::from_f(0.f);
+  }
+
+  const int64_t Ttot = tile0[a.batch];
+  const int grid = gridDim.x;
+  const int u0 = range_start(blockIdx.x, Ttot, grid);
+  const int u1 = range_start(blockIdx.x + 1, Ttot, grid);
+  if (u0 >= u1) return;
 
   if (warp == kWarps) {
     // ------------------------------------------------------------ producer
     if (lane != 0) return;
     const uint64_t pol = policy_evict_first();
-    ItemWalker w(a);
-    w.advance(blockIdx.x);
-    int j = 0;
-    for (; w.valid(); w.advance(gridDim.x)) {
-      const Item it = w.get();
-      for (int t0 = 0; t0 < it.ntok; t0 += kTile, ++j) {
-        const int s = j % a.nstages;
-        if (j >= a.nstages && !mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty))
-          return;
-        const int n = min(kTile, it.ntok - t0);
+    if constexpr (kMma) { prefetch_tmap(&a.kmap); prefetch_tmap(&a.vmap); }
+    TileWalker w(a, tile0, u0);
+    for (int u = u0, j = 0; u < u1; ++u, ++j, w.next()) {
+      const int s = j % a.nstages;
+      if (j >= a.nstages && !mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty))
+        return;
+      const int n = w.ntok();
+      uint8_t* dk = smem + (size_t)s * kStage;
+      uint8_t* dv = dk + kStage / 2;
+      if constexpr (kMma) {
+        // boxes of 16 tokens x 64 dims; both dim halves of K and of V
+        int boxes = 0;
+        for (int t = 0; t < n; t += kBoxRows) ++boxes;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(boxes * 4 * kBoxRows * 128));
+        for (int t = 0; t < n; t += kBoxRows) {
+          int run;
+          const int64_t r = kv_rowidx(a, w.b, w.hk, w.tt * kTile + t, &run);
+          for (int h = 0; h < 2; ++h) {
+            tma_load_2d(dk + h * kHalf + t * 128, &a.kmap, h * 64, (int)r, &full[s], pol);
+            tma_load_2d(dv + h * kHalf + t * 128, &a.vmap, h * 64, (int)r, &full[s], pol);
+          }
+        }
+      } else {
         mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * n * kD * sizeof(T)));
-        uint8_t* dk = smem + (size_t)s * kStage;
-        uint8_t* dv = dk + kTile * kD * sizeof(T);
+        const T* K = static_cast<const T*>(a.k);
+        const T* V = static_cast<const T*>(a.v);
         for (int t = 0; t < n;) {
           int run;
-          const T* ks = kv_row<T>(a, a.k, it.b, it.hk, it.t0 + t0 + t, &run);
-          const T* vs = kv_row<T>(a, a.v, it.b, it.hk, it.t0 + t0 + t, &run);
+          const int64_t r = kv_rowidx(a, w.b, w.hk, w.tt * kTile + t, &run);
           const int m = min(run, n - t);
           const uint32_t bytes = (uint32_t)(m * kD * sizeof(T));
-          bulk_g2s(dk + (size_t)t * kD * sizeof(T), ks, bytes, &full[s], pol);
-          bulk_g2s(dv + (size_t)t * kD * sizeof(T), vs, bytes, &full[s], pol);
+          bulk_g2s(dk + (size_t)t * kD * sizeof(T), K + r * kD, bytes, &full[s], pol);
+          bulk_g2s(dv + (size_t)t * kD * sizeof(T), V + r * kD, bytes, &full[s], pol);
           t += m;
         }
       }
@@ -168,45 +231,152 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const FdArgs a
   const T* q = static_cast<const T*>(a.q);
   T* out = static_cast<T*>(a.out);
 
-  // Sequences of length 0 have no items: their output is defined as zeros.
-  if (blockIdx.x == 0 && a.lens != nullptr) {
-    for (int b = 0; b < a.batch; ++b)
-      if (seq_len(a, b) == 0)
-        for (int i = tid; i < a.hq * kD; i += kConsumers)
-          out[(size_t)b * a.hq * kD + i] = Elem<T>::from_f(0.f);
-  }
+  // Per-warp online-softmax state. CUDA-core path: lane owns dims 4l..4l+3 of
+  // each of the G heads. Tensor-core path: lane owns head r = lane/4 and dims
+  // 8*nd + 2*(lane%4) + {0,1} for nd < 16.
+  constexpr int kO = kMma ? 32 : 4 * G;
+  constexpr int kS = kMma ? 1 : G;
+  float o[kO], m[kS], l[kS];
+  float qr[kMma ? 1 : G][4];
+  uint32_t qa[kMma ? 8 : 1][2];     // A fragments of Q (rows 0..7 = heads), 8 k-steps
+  const int grp = warp >> 2, wi = warp & 3;
+  const int r_head = lane >> 2;     // tensor-core path: this lane's head row
 
-  ItemWalker w(a);
-  w.advance(blockIdx.x);
-  int j = 0;
-  for (; w.valid(); w.advance(gridDim.x)) {
-    const Item it = w.get();
-    // q for the G heads sharing this kv head, dims 4*lane..4*lane+3, pre-scaled.
-    float qr[G][4];
+  TileWalker w(a, tile0, u0);
+  int seg_first = u0;
+  for (int u = u0, j = 0; u < u1; ++u, ++j, w.next()) {
+    const int s = j % a.nstages;
+    const bool seg_begin = (u == u0) || (w.tt == 0);
+    const bool seg_end = (u == u1 - 1) || (w.tt == w.ntb - 1);
+    if (seg_begin) {
+      seg_first = u;
+      const T* qb = q + ((size_t)w.b * a.hq + (size_t)w.hk * G) * kD;
+      if constexpr (kMma) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const T* qp = q + ((size_t)it.b * a.hq + it.hk * G + g) * kD + 4 * lane;
-      const uint2 raw = *reinterpret_cast<const uint2*>(qp);
-      const float2 lo = Elem<T>::unpack2(raw.x), hi = Elem<T>::unpack2(raw.y);
-      qr[g][0] = lo.x * a.qscale; qr[g][1] = lo.y * a.qscale;
-      qr[g][2] = hi.x * a.qscale; qr[g][3] = hi.y * a.qscale;
-    }
-    float m[G], l[G], o[G][4];
+        for (int kk = 0; kk < 8; ++kk) {
+          if (r_head < G) {
+            const T* qp = qb + (size_t)r_head * kD + kk * 16 + 2 * (lane & 3);
+            qa[kk][0] = *reinterpret_cast<const uint32_t*>(qp);
+            qa[kk][1] = *reinterpret_cast<const uint32_t*>(qp + 8);
+          } else {
+            qa[kk][0] = qa[kk][1] = 0u;
+          }
+        }
+        m[0] = -INFINITY; l[0] = 0.f;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      m[g] = -INFINITY; l[g] = 0.f;
-      o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+        for (int e = 0; e < kO; ++e) o[e] = 0.f;
+      } else {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(qb + (size_t)g * kD + 4 * lane);
+          const float2 lo = Elem<T>::unpack2(raw.x), hi = Elem<T>::unpack2(raw.y);
+          qr[g][0] = lo.x * a.qscale; qr[g][1] = lo.y * a.qscale;
+          qr[g][2] = hi.x * a.qscale; qr[g][3] = hi.y * a.qscale;
+          m[g] = -INFINITY; l[g] = 0.f;
+          o[4 * g] = o[4 * g + 1] = o[4 * g + 2] = o[4 * g + 3] = 0.f;
+        }
+      }
     }
 
-    for (int t0 = 0; t0 < it.ntok; t0 += kTile, ++j) {
-      const int s = j % a.nstages;
+    const int n = w.ntok();
+    const uint32_t kst = smem_u32(smem + (size_t)s * kStage);
+    const uint32_t vst = kst + kStage / 2;
+    if constexpr (kMma) {
+      if ((j & 1) == grp) {
+        if (!mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull)) return;
+        const int t0 = wi * 16;                 // this warp's 16 tokens
+        if (t0 < n) {
+          if (n < kTile && t0 + 16 > n) {
+            // ragged tail: zero this warp's V rows >= n (their probabilities are 0,
+            // but the rows may hold stale or out-of-sequence data)
+            for (int r = max(n, t0); r < t0 + 16; ++r) {
+              uint8_t* p0 = smem + (size_t)s * kStage + kStage / 2 + r * 128;
+              reinterpret_cast<uint4*>(p0)[lane & 7] = make_uint4(0, 0, 0, 0);
+              reinterpret_cast<uint4*>(p0 + kHalf)[lane & 7] = make_uint4(0, 0, 0, 0);
+            }
+            fence_proxy_async_smem();   // order these writes before the next TMA refill
+            __syncwarp();
+          }
+          // S[16 heads x 16 tokens] = Q K^T as two n-tiles of 8 tokens
+          float sc[2][4];
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+            const int tok = t0 + nt * 8 + (lane & 7);
+#pragma unroll
+            for (int kp = 0; kp < 4; ++kp) {        // pairs of k-steps: 32 dims
+              const int chunk = kp * 4 + (lane >> 3);     // 16-byte chunk of the 256-byte row
+              const int h = chunk >> 3, c = chunk & 7;
+              uint32_t kb[4];
+              ldsm_x4(kst + h * kHalf + tok * 128 + ((c ^ (tok & 7)) << 4), kb);
+              Mma<T>::run(sc[nt], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, kb[0], kb[1]);
+              Mma<T>::run(sc[nt], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, kb[2], kb[3]);
+            }
+          }
+          // online softmax on row r_head (fragment elements 0, 1 of each n-tile)
+          float mx = m[0];
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int tok = t0 + nt * 8 + 2 * (lane & 3) + e;
+              const float v = (tok < n) ? sc[nt][e] * a.qscale : -INFINITY;
+              sc[nt][e] = v;
+              mx = fmaxf(mx, v);
+            }
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          const float alpha = exp2f(m[0] - mx);
+          m[0] = mx;
+          float ls = 0.f;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              sc[nt][e] = exp2f(sc[nt][e] - mx);
+              ls += sc[nt][e];
+            }
+          l[0] = l[0] * alpha + ls;             // lane-partial row sum
+#pragma unroll
+          for (int e = 0; e < kO; ++e) o[e] *= alpha;
+          // P as A fragments (rows 8..15 are zero): high and low 16-bit parts
+          const uint32_t ph0 = Mma<T>::pack(sc[0][0], sc[0][1]);
+          const uint32_t ph2 = Mma<T>::pack(sc[1][0], sc[1][1]);
+          uint32_t pl0 = 0u, pl2 = 0u;
+          if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+            const float2 h0 = Elem<T>::unpack2(ph0), h2 = Elem<T>::unpack2(ph2);
+            pl0 = Mma<T>::pack(sc[0][0] - h0.x, sc[0][1] - h0.y);
+            pl2 = Mma<T>::pack(sc[1][0] - h2.x, sc[1][1] - h2.y);
+          }
+          // O[16 x 128] += P[16 x 16 tokens] V[16 tokens x 128]
+#pragma unroll
+          for (int np = 0; np < 8; ++np) {          // pairs of 8-dim n-tiles
+            const int tok = t0 + ((lane >> 3) & 1) * 8 + (lane & 7);
+            const int chunk = np * 2 + (lane >> 4);
+            const int h = chunk >> 3, c = chunk & 7;
+            uint32_t vb[4];
+            ldsm_x4_t(vst + h * kHalf + tok * 128 + ((c ^ (tok & 7)) << 4), vb);
+            float d0[4] = {o[4 * np], o[4 * np + 1], 0.f, 0.f};
+            float d1[4] = {o[4 * np + 2], o[4 * np + 3], 0.f, 0.f};
+            Mma<T>::run(d0, ph0, 0u, ph2, 0u, vb[0], vb[1]);
+            Mma<T>::run(d1, ph0, 0u, ph2, 0u, vb[2], vb[3]);
+            if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+              Mma<T>::run(d0, pl0, 0u, pl2, 0u, vb[0], vb[1]);
+              Mma<T>::run(d1, pl0, 0u, pl2, 0u, vb[2], vb[3]);
+            }
+            o[4 * np] = d0[0]; o[4 * np + 1] = d0[1];
+            o[4 * np + 2] = d1[0]; o[4 * np + 3] = d1[1];
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+    } else {
       if (!mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull)) return;
-      const int n = min(kTile, it.ntok - t0);
       const int mine = min(8, n - warp * 8);           // tokens of this warp
       if (mine > 0) {
-        const uint32_t kbase = smem_u32(smem + (size_t)s * kStage) +
-                               (uint32_t)((warp * 8) * kD + 4 * lane) * sizeof(T);
-        const uint32_t vbase = kbase + kTile * kD * sizeof(T);
+        const uint32_t kbase = kst + (uint32_t)((warp * 8) * kD + 4 * lane) * sizeof(T);
+        const uint32_t vbase = kbase + kStage / 2;
         float sc[8][G];
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
@@ -233,13 +403,13 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const FdArgs a
           float mx = m[g];
 #pragma unroll
           for (int t = 0; t < 8; ++t) mx = fmaxf(mx, sc[t][g]);
-          const float alpha = exp2f(m[g] - mx);   // 0 on the first tile (m = -inf)
+          const float alpha = exp2f(m[g] - mx);
           m[g] = mx;
           l[g] *= alpha;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) o[g][e] *= alpha;
+          for (int e = 0; e < 4; ++e) o[4 * g + e] *= alpha;
 #pragma unroll
-          for (int t = 0; t < 8; ++t) sc[t][g] = exp2f(sc[t][g] - mx);   // -inf -> 0
+          for (int t = 0; t < 8; ++t) sc[t][g] = exp2f(sc[t][g] - mx);
         }
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
@@ -252,10 +422,10 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const FdArgs a
             for (int g = 0; g < G; ++g) {
               const float p = sc[t][g];
               l[g] += p;
-              o[g][0] = fmaf(p, v01.x, o[g][0]);
-              o[g][1] = fmaf(p, v01.y, o[g][1]);
-              o[g][2] = fmaf(p, v23.x, o[g][2]);
-              o[g][3] = fmaf(p, v23.y, o[g][3]);
+              o[4 * g] = fmaf(p, v01.x, o[4 * g]);
+              o[4 * g + 1] = fmaf(p, v01.y, o[4 * g + 1]);
+              o[4 * g + 2] = fmaf(p, v23.x, o[4 * g + 2]);
+              o[4 * g + 3] = fmaf(p, v23.y, o[4 * g + 3]);
             }
           }
         }
@@ -263,18 +433,35 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const FdArgs a
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
+    if (!seg_end) continue;
 
-    // ---- merge the 8 warps' states for this item
-    named_bar_sync(1, kConsumers);   // previous item's readers of mrg are done
+    // ---- segment done: merge the 8 warps' states in shared memory
+    named_bar_sync(1, kConsumers);     // readers of the previous segment's mrg are done
+    if constexpr (kMma) {
+      float lsum = l[0];
+      lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+      lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+      if (r_head < G) {
+        float* dst = mrg + (warp * G + r_head) * kMrg;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float* dst = mrg + (warp * G + g) * kMrg;
-      *reinterpret_cast<float4*>(dst + 4 * lane) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
-      if (lane == 0) { dst[kD] = m[g]; dst[kD + 1] = l[g]; }
+        for (int nd = 0; nd < 16; ++nd)
+          *reinterpret_cast<float2*>(dst + nd * 8 + 2 * (lane & 3)) =
+              make_float2(o[2 * nd], o[2 * nd + 1]);
+        if ((lane & 3) == 0) { dst[kD] = m[0]; dst[kD + 1] = lsum; }
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float* dst = mrg + (warp * G + g) * kMrg;
+        *reinterpret_cast<float4*>(dst + 4 * lane) =
+            make_float4(o[4 * g], o[4 * g + 1], o[4 * g + 2], o[4 * g + 3]);
+        if (lane == 0) { dst[kD] = m[g]; dst[kD + 1] = l[g]; }
+      }
     }
     named_bar_sync(1, kConsumers);
-    const bool single = (it.nsplit == 1);
-    const int item_id = ((it.b * a.hkv + it.hk) * a.items_per_seqhead) + it.s;
+    const int rs = w.row_start();
+    const bool whole = (seg_first == rs) && (w.tt == w.ntb - 1);
+    const int slot = 2 * blockIdx.x + (seg_first == u0 ? 0 : 1);
     for (int idx = tid; idx < G * kD; idx += kConsumers) {
       const int g = idx / kD, d = idx - g * kD;
       float M = -INFINITY;
@@ -284,87 +471,69 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const FdArgs a
 #pragma unroll
       for (int ww = 0; ww < kWarps; ++ww) {
         const float* src = mrg + (ww * G + g) * kMrg;
-        const float f = exp2f(src[kD] - M);   // warps without tokens: m = -inf -> 0
+        const float f = (src[kD + 1] > 0.f) ? exp2f(src[kD] - M) : 0.f;
         L = fmaf(f, src[kD + 1], L);
         O = fmaf(f, src[d], O);
       }
-      if (single) {
-        out[((size_t)it.b * a.hq + it.hk * G + g) * kD + d] = Elem<T>::from_f(O / L);
+      if (whole) {
+        out[((size_t)w.b * a.hq + (size_t)w.hk * G + g) * kD + d] = Elem<T>::from_f(O / L);
       } else {
-        a.part_o[((size_t)item_id * G + g) * kD + d] = O;
-        if (d == 0) a.part_ml[(size_t)item_id * G + g] = make_float2(M, L);
+        a.part_o[((size_t)slot * G + g) * kD + d] = O;
+        if (d == 0) a.part_ml[(size_t)slot * G + g] = make_float2(M, L);
       }
     }
-    if (single) continue;
+    if (whole) continue;
 
-    // ---- publish the partial; the last split of (b, hk) to arrive merges all
+    // ---- publish the partial; the last CTA of this row to arrive merges them
     __threadfence();
     named_bar_sync(1, kConsumers);
-    __shared__ int last;
+    const int row_end = rs + w.ntb - 1;
+    const int c_first = owner(rs, Ttot, grid), c_last = owner(row_end, Ttot, grid);
     if (tid == 0) {
-      const int prev = atomicAdd(&a.done[it.b * a.hkv + it.hk], 1);
-      last = (prev == it.nsplit - 1);
+      const int prev = atomicAdd(&a.done[w.row()], 1);
+      s_last = (prev == c_last - c_first);
     }
     named_bar_sync(1, kConsumers);
-    if (!last) continue;
+    if (!s_last) continue;
     __threadfence();
-    const int base = (it.b * a.hkv + it.hk) * a.items_per_seqhead;
     for (int idx = tid; idx < G * kD; idx += kConsumers) {
       const int g = idx / kD, d = idx - g * kD;
       float M = -INFINITY;
-      for (int sp = 0; sp < it.nsplit; ++sp)
-        M = fmaxf(M, __ldcg(&a.part_ml[(size_t)(base + sp) * G + g].x));
+      for (int c = c_first; c <= c_last; ++c) {
+        const int sl = 2 * c + (range_start(c, Ttot, grid) >= rs ? 0 : 1);
+        M = fmaxf(M, __ldcg(&a.part_ml[(size_t)sl * G + g].x));
+      }
       float L = 0.f, O = 0.f;
-      for (int sp = 0; sp < it.nsplit; ++sp) {
-        const float2 ml = __ldcg(&a.part_ml[(size_t)(base + sp) * G + g]);
+      for (int c = c_first; c <= c_last; ++c) {
+        const int sl = 2 * c + (range_start(c, Ttot, grid) >= rs ? 0 : 1);
+        const float2 ml = __ldcg(&a.part_ml[(size_t)sl * G + g]);
         const float f = exp2f(ml.x - M);
         L = fmaf(f, ml.y, L);
-        O = fmaf(f, __ldcg(&a.part_o[((size_t)(base + sp) * G + g) * kD + d]), O);
+        O = fmaf(f, __ldcg(&a.part_o[((size_t)sl * G + g) * kD + d]), O);
       }
-      out[((size_t)it.b * a.hq + it.hk * G + g) * kD + d] = Elem<T>::from_f(O / L);
+      out[((size_t)w.b * a.hq + (size_t)w.hk * G + g) * kD + d] = Elem<T>::from_f(O / L);
     }
-    if (tid == 0) a.done[it.b * a.hkv + it.hk] = 0;   // ready for the next launch
+    if (tid == 0) a.done[w.row()] = 0;   // ready for the next launch
   }
 }
 
-struct FdPlan {
-  int split_tokens, items_per_seqhead;
-  size_t items_cap;
-};
-
-FdPlan plan(int batch, int hkv, int max_len, int split_tokens, int num_sms) {
-  FdPlan p{};
-  int st = split_tokens;
-  if (st <= 0) {
-    // ~16 items per SM if every sequence had max_len tokens.
-    const int64_t total = (int64_t)batch * hkv * max_len;
-    const int64_t per = (total + (int64_t)num_sms * 16 - 1) / ((int64_t)num_sms * 16);
-    st = (int)((per + kTile - 1) / kTile) * kTile;
-    if (st < kTile) st = kTile;
-  }
-  p.split_tokens = st;
-  p.items_per_seqhead = (max_len + st - 1) / st;
-  p.items_cap = (size_t)batch * hkv * p.items_per_seqhead;
-  return p;
-}
-
-size_t ws_bytes_for(const FdPlan& p, int batch, int hq, int hkv) {
+size_t ws_bytes_for(int grid, int batch, int hq, int hkv) {
   const int G = hq / hkv;
-  size_t b = 0;
-  b += p.items_cap * G * kD * sizeof(float);      // part_o
-  b += p.items_cap * G * sizeof(float2);          // part_ml
-  b += (size_t)batch * hkv * sizeof(int);         // done counters
+  size_t b = (size_t)2 * grid * G * kD * sizeof(float);   // part_o
+  b += (size_t)2 * grid * G * sizeof(float2);             // part_ml
+  b += (size_t)batch * hkv * sizeof(int);                 // done counters
   return (b + 255) & ~(size_t)255;
 }
 
 template <typename T, int G>
 int launch_g(FdArgs a, cudaStream_t st, const DeviceInfo& dev, int grid) {
   constexpr int kStage = 2 * kTile * kD * (int)sizeof(T);
-  const size_t fixed = (size_t)kWarps * G * kMrg * 4 + G * 8 + 64;
+  const size_t fixed = 1024 + (size_t)kWarps * G * kMrg * 4 + (size_t)(a.batch + 1) * 4 + 64;
   int nst = kMaxStages;
   while (nst > 2 && (size_t)nst * (kStage + 16) + fixed > (size_t)dev.max_smem_optin - 1024) --nst;
   a.nstages = nst;
   const size_t smem = (size_t)nst * (kStage + 16) + fixed;
+  if (smem > (size_t)dev.max_smem_optin) return DBK_ESHAPE;
   auto kern = flashdecode_kernel<T, G>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
@@ -389,12 +558,13 @@ using namespace dbk;
 
 extern "C" size_t dbk_flashdecode_workspace_bytes(int batch, int n_q_heads, int n_kv_heads,
                                                   int max_len, int split_tokens) {
+  (void)max_len;
+  (void)split_tokens;
   if (batch < 1 || n_kv_heads < 1 || n_q_heads < n_kv_heads || max_len < 1) return 0;
   DeviceInfo dev;
   int nsm = 148;
   if (current_device_info(&dev) == DBK_OK) nsm = dev.num_sms;
-  const FdPlan p = plan(batch, n_kv_heads, max_len, split_tokens, nsm);
-  return ws_bytes_for(p, batch, n_q_heads, n_kv_heads);
+  return ws_bytes_for(nsm, batch, n_q_heads, n_kv_heads);
 }
 
 extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v_cache,
@@ -405,24 +575,28 @@ extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v
                                size_t workspace_bytes, void* stream) {
   if (!q || !k_cache || !v_cache || !out) return DBK_ENULL;
   if (dtype != DBK_F16 && dtype != DBK_BF16) return DBK_EDTYPE;
-  if (head_dim != kD || batch < 1 || n_kv_heads < 1 || n_q_heads < n_kv_heads ||
-      n_q_heads % n_kv_heads != 0 || max_len < 1)
+  if (head_dim != kD || batch < 1 || batch > kMaxBatchSmem || n_kv_heads < 1 ||
+      n_q_heads < n_kv_heads || n_q_heads % n_kv_heads != 0 || max_len < 1)
     return DBK_ESHAPE;
   const int G = n_q_heads / n_kv_heads;
   if (G != 1 && G != 2 && G != 4 && G != 8) return DBK_ESHAPE;
-  if (split_tokens < 0 || split_tokens % kTile != 0) return DBK_ESHAPE;
+  if (split_tokens < 0) return DBK_ESHAPE;
   if (page_table) {
     if (page_size < 1 || max_pages_per_seq < 1 ||
         (int64_t)page_size * max_pages_per_seq < max_len)
       return DBK_ESHAPE;
+    if (G >= 4 && page_size % kBoxRows != 0) return DBK_ESHAPE;
   }
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
     return DBK_EALIGN;
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc) return rc;
-  const FdPlan p = plan(batch, n_kv_heads, max_len, split_tokens, dev.num_sms);
-  const size_t need = ws_bytes_for(p, batch, n_q_heads, n_kv_heads);
+  // Grid: one CTA per SM, or fewer when there are fewer tiles than SMs
+  // (an upper bound on tiles: every sequence at max_len).
+  const int64_t max_tiles = (int64_t)batch * n_kv_heads * ((max_len + kTile - 1) / kTile);
+  const int grid = (int)(max_tiles < dev.num_sms ? max_tiles : dev.num_sms);
+  const size_t need = ws_bytes_for(dev.num_sms, batch, n_q_heads, n_kv_heads);
   if (!workspace || workspace_bytes < need) return DBK_EWORKSPACE;
   if (!aligned16(workspace)) return DBK_EALIGN;
 
@@ -430,17 +604,27 @@ extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v
   a.q = q; a.k = k_cache; a.v = v_cache; a.pages = page_table; a.lens = seq_lens; a.out = out;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   a.part_o = reinterpret_cast<float*>(ws);
-  ws += p.items_cap * G * kD * sizeof(float);
+  ws += (size_t)2 * dev.num_sms * G * kD * sizeof(float);
   a.part_ml = reinterpret_cast<float2*>(ws);
-  ws += p.items_cap * G * sizeof(float2);
+  ws += (size_t)2 * dev.num_sms * G * sizeof(float2);
   a.done = reinterpret_cast<int*>(ws);
   a.batch = batch; a.hq = n_q_heads; a.hkv = n_kv_heads; a.max_len = max_len;
   a.page_size = page_table ? page_size : max_len;
   a.max_pages = page_table ? max_pages_per_seq : 1;
-  a.split_tokens = p.split_tokens;
-  a.items_per_seqhead = p.items_per_seqhead;
   a.qscale = scale * kLog2e;
-  const int grid = (int)((p.items_cap < (size_t)dev.num_sms) ? p.items_cap : dev.num_sms);
+  if (G >= 4) {
+    // 2-D views [rows, 128] of the caches for the tensor-core path's TMA boxes.
+    // Contiguous caches: exact extent, so a box overhanging the end of the cache
+    // reads zeros. Paged caches: the page count is not an argument; every box
+    // (16 rows, page_size % 16 == 0, box-aligned within its page) stays inside
+    // one page of the table, so the view's extent only needs to cover them.
+    const uint64_t prow = page_table ? (((uint64_t)1 << 31) - 1)
+                                     : (uint64_t)batch * n_kv_heads * max_len;
+    rc = encode_tmap_2d(&a.kmap, k_cache, dtype, kD, prow, kD * 2, 64, kBoxRows, true);
+    if (rc) return rc;
+    rc = encode_tmap_2d(&a.vmap, v_cache, dtype, kD, prow, kD * 2, 64, kBoxRows, true);
+    if (rc) return rc;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == DBK_F16 ? launch_t<__half>(a, G, st, dev, grid)
                           : launch_t<__nv_bfloat16>(a, G, st, dev, grid);
