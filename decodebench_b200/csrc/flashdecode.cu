@@ -176,11 +176,13 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
           out[(size_t)b * a.hq * kD + i] = Elem<T>::from_f(0.f);
   }
 
+  // Effective grid: never more CTAs than tiles, so every range is non-empty and
+  // the CTAs covering a row are exactly owner(first tile) .. owner(last tile).
   const int64_t Ttot = tile0[a.batch];
-  const int grid = gridDim.x;
+  if (Ttot == 0 || blockIdx.x >= Ttot) return;
+  const int grid = (int)min((int64_t)gridDim.x, Ttot);
   const int u0 = range_start(blockIdx.x, Ttot, grid);
   const int u1 = range_start(blockIdx.x + 1, Ttot, grid);
-  if (u0 >= u1) return;
 
   if (warp == kWarps) {
     // ------------------------------------------------------------ producer
