@@ -32,6 +32,8 @@ SIGNATURES = {
     "dbk_gemv": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
     "dbk_flashdecode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,
                              _P, _SZ, _P]),
+    "dbk_flashdecode_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I,
+                                     _P]),
 }
 
 _lib = None

@@ -26,6 +26,7 @@
 //     warps take alternate stages, each warp 16 tokens: S = Q K^T (fp32
 //     accumulate), online softmax in registers, O += P V with P split into a
 //     high and a low 16-bit part so the probabilities keep fp32-like accuracy.
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -630,4 +631,73 @@ extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == DBK_F16 ? launch_t<__half>(a, G, st, dev, grid)
                           : launch_t<__nv_bfloat16>(a, G, st, dev, grid);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory at all: plugins loaded into a
+// host process whose allocator owns the whole device (no cudaMalloc allowed,
+// no torch allocator available), or code running where an allocation would
+// break a fixed memory budget. dbk_flashdecode needs a scratch workspace; this
+// variant takes it from a fixed array compiled into the library instead.
+//
+// The array lives in every GPU that loads the library, until the process
+// exits. Its address is looked up once per device (cudaGetSymbolAddress) on
+// the first call made with that device current, so that first call should
+// come before any stream capture. All calls share the one array: calls that
+// overlap on the GPU (different streams, different threads) race and give
+// wrong results. Each call clears the arrival counters it uses before the
+// kernel runs.
+namespace {
+constexpr size_t kNoAllocScratchBytes = (size_t)2 << 20;   // 2 MiB
+static __device__ __align__(256) uint8_t g_fd_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevicesNoAlloc = 64;
+void* g_fd_scratch_ptr[kMaxDevicesNoAlloc];
+std::mutex g_fd_scratch_mu;
+
+int scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevicesNoAlloc) return DBK_EDEVICE;
+  std::lock_guard<std::mutex> lk(g_fd_scratch_mu);
+  if (g_fd_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_fd_scratch);
+    if (e != cudaSuccess) return (int)e;
+    g_fd_scratch_ptr[dev] = p;
+  }
+  *out = g_fd_scratch_ptr[dev];
+  return DBK_OK;
+}
+}  // namespace
+
+extern "C" int dbk_flashdecode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                       const int32_t* page_table, const int32_t* seq_lens,
+                                       void* out, int batch, int n_q_heads, int n_kv_heads,
+                                       int head_dim, int max_len, int page_size,
+                                       int max_pages_per_seq, float scale, int dtype,
+                                       void* stream) {
+  if (batch < 1 || n_kv_heads < 1 || n_q_heads < n_kv_heads || max_len < 1) return DBK_ESHAPE;
+  const size_t need = dbk_flashdecode_workspace_bytes(batch, n_q_heads, n_kv_heads, max_len, 0);
+  if (need == 0 || need > kNoAllocScratchBytes) return DBK_EWORKSPACE;
+  void* ws = nullptr;
+  int rc = scratch_address(&ws);
+  if (rc) return rc;
+  // The arrival counters sit at the end of the workspace layout; start them at zero.
+  const size_t counters = (size_t)batch * n_kv_heads * sizeof(int);
+  const size_t G = (size_t)(n_q_heads / n_kv_heads);
+  DeviceInfo dev;
+  rc = current_device_info(&dev);
+  if (rc) return rc;
+  const size_t off = (size_t)2 * dev.num_sms * G * kD * sizeof(float) +
+                     (size_t)2 * dev.num_sms * G * sizeof(float2);
+  cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(ws) + off, 0, counters,
+                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return (int)e;
+  return dbk_flashdecode(q, k_cache, v_cache, page_table, seq_lens, out, batch, n_q_heads,
+                         n_kv_heads, head_dim, max_len, page_size, max_pages_per_seq, scale, 0,
+                         dtype, ws, kNoAllocScratchBytes, stream);
 }

@@ -115,6 +115,23 @@ int dbk_flashdecode(const void* q, const void* k_cache, const void* v_cache,
                     int page_size, int max_pages_per_seq, float scale, int split_tokens,
                     int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* dbk_flashdecode without a caller workspace, for callers that cannot allocate
+ * device memory (for example a plugin inside a host process whose own
+ * allocator owns the GPU, so it may not call cudaMalloc or a framework
+ * allocator). No counterpart in the reference: it is an addition of this
+ * library. Same arguments and results as dbk_flashdecode (automatic split), but
+ * the scratch comes from a 2 MiB array compiled into the library and held on
+ * every GPU that loads it until the process exits. Sizes whose workspace
+ * (dbk_flashdecode_workspace_bytes) exceeds 2 MiB return DBK_EWORKSPACE.
+ * The first call on a device looks up the array's device address and should
+ * come before any stream capture. All calls share the array: calls that
+ * overlap on the GPU race. Allocates nothing. */
+int dbk_flashdecode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                            const int32_t* page_table, const int32_t* seq_lens, void* out,
+                            int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len,
+                            int page_size, int max_pages_per_seq, float scale, int dtype,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif
