@@ -29,6 +29,8 @@
 // (validation/src/kernels/fused/f1.cu:18-84, f2.cu:17-76) and the Python stages
 // (src/decodebench/demos/llama_decode.py:36-43, :77-87): fp32 accumulation,
 // silu(g) = g / (1 + exp(-g)) (f2.cu:73), output rounded once to fp16/bf16.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "dbk_internal.h"
 
@@ -255,6 +257,250 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(const GemvArgs
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core variant (d_in % 16 == 0, activations fit in shared memory).
+//
+// On CUDA cores the stream above is issue-bound on 16-bit -> fp32 conversions
+// (16K per 32 KB stage at quarter rate). Here the weights go from shared memory
+// straight into mma.m16n8k16 (fp32 accumulation) through ldmatrix, so no
+// per-weight conversion or FMA is issued:
+//   * a stage is one m-tile of 16 weight rows x KC = 2048 columns; each row
+//     segment (4 KB) is one cp.async.bulk into a slot padded to 4112 bytes, so
+//     the 8 rows of an ldmatrix 8x8 block fall in 8 different bank groups.
+//     Segments of 4 KB or more keep DRAM near its streaming rate when they come
+//     from different rows; 2 KB segments measured ~30% slower;
+//   * warp w owns columns [256 w, 256 w + 256) of every stage (16 k-steps); its
+//     fp32 partial of the m-tile stays in the mma accumulator across the K
+//     chunks and is written once per m-tile to a per-warp buffer; the epilogue
+//     sums the 8 warp partials in a fixed order (deterministic);
+//   * the activation is the B operand (N = 8 columns = the batch, up to 8):
+//     x * gamma is staged in shared memory as a high and a low 16-bit part and
+//     both are multiplied, so x * gamma keeps ~22 (fp16) / ~16 (bf16) bits;
+//   * SwiGLU: an m-tile holds 8 gate rows (rows 0..7) and the 8 up rows of the
+//     same outputs (rows 8..15), so the epilogue reads gate and up of an output
+//     from neighbouring partial rows.
+constexpr int kMmaKC = 2048;
+constexpr int kMmaSlot = kMmaKC * 2 + 16;     // padded row slot (bytes)
+constexpr int kMmaStage = 16 * kMmaSlot;      // 65,792 bytes
+constexpr int kMmaStages = 3;
+
+template <typename T, int MODE, bool SPLIT>
+__global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a) {
+  constexpr int NMAT = (MODE == MODE_SWIGLU) ? 2 : 1;
+  constexpr int RPT = 16 / NMAT;                  // output rows per m-tile
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* ring = smem_raw;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)a.nstages * kMmaStage);
+  uint64_t* empty = full + a.nstages;
+  const int nmt_max = (a.max_rows + RPT - 1) / RPT;
+  float* part = reinterpret_cast<float*>(empty + a.nstages);   // [8 warps][nmt_max*16][batch]
+  uint16_t* xs_hi = reinterpret_cast<uint16_t*>(part + (size_t)kConsumerWarps * nmt_max * 16 * a.batch);
+  uint16_t* xs_lo = xs_hi + (size_t)a.batch * a.d_in;
+  __shared__ float red[kConsumerWarps][8];
+  __shared__ float inv_rms[8];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x;
+  const int row0 = (int)(((int64_t)blockIdx.x * a.d_out) / G);
+  const int row1 = (int)(((int64_t)(blockIdx.x + 1) * a.d_out) / G);
+  const int nrows = row1 - row0;
+  const int nmt = (nrows + RPT - 1) / RPT;
+  const int total = nmt * a.nchunks;
+
+  if (tid == 0) {
+    for (int s = 0; s < a.nstages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;");
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const T* W0 = static_cast<const T*>(a.w0);
+      const T* W1 = static_cast<const T*>(a.w1);
+      for (int j = 0; j < total; ++j) {
+        const int s = j % a.nstages;
+        if (j >= a.nstages &&
+            !mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty))
+          return;
+        const int mt = j / a.nchunks, c = j - mt * a.nchunks;
+        const int col0 = c * kMmaKC;
+        const int seg = min(kMmaKC, a.d_in - col0);
+        const int r_first = row0 + mt * RPT;
+        const int valid = min(RPT, row1 - r_first);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(valid * NMAT * seg * sizeof(T)));
+        uint8_t* dst = ring + (size_t)s * kMmaStage;
+        for (int q = 0; q < valid; ++q) {
+          const size_t off = (size_t)(r_first + q) * a.d_in + col0;
+          bulk_g2s(dst + q * kMmaSlot, W0 + off, (uint32_t)(seg * sizeof(T)), &full[s], pol);
+          if constexpr (NMAT == 2)
+            bulk_g2s(dst + (8 + q) * kMmaSlot, W1 + off, (uint32_t)(seg * sizeof(T)), &full[s], pol);
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const T* x = static_cast<const T*>(a.x);
+  const T* gam = static_cast<const T*>(a.gamma);
+  {
+    // Stage x (* gamma) as high + low 16-bit parts; sum(x^2) in the same pass.
+    float ss[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) ss[b] = 0.f;
+    const int per_row = a.d_in / 8;
+    for (int v = tid; v < a.batch * per_row; v += kConsumers) {
+      const int b = v / per_row, c = (v - b * per_row) * 8;
+      float f[8], g[8];
+      unpack8<T>(ldg_nc_v4(x + (size_t)b * a.d_in + c), f);
+      if (gam != nullptr) unpack8<T>(ldg_nc_v4(gam + c), g);
+      uint32_t hi[4], lo[4];
+      float sq = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        float p0 = f[e], p1 = f[e + 1];
+        sq = fmaf(p0, p0, fmaf(p1, p1, sq));
+        if (gam != nullptr) { p0 *= g[e]; p1 *= g[e + 1]; }
+        hi[e / 2] = Mma<T>::pack(p0, p1);
+        const float2 h = Elem<T>::unpack2(hi[e / 2]);
+        lo[e / 2] = Mma<T>::pack(p0 - h.x, p1 - h.y);
+      }
+#pragma unroll
+      for (int bb = 0; bb < 8; ++bb) ss[bb] += (bb == b) ? sq : 0.f;
+      *reinterpret_cast<uint4*>(xs_hi + (size_t)b * a.d_in + c) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(xs_lo + (size_t)b * a.d_in + c) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const float t = warp_sum(ss[b]);
+      if (lane == 0) red[warp][b] = t;
+    }
+  }
+  named_bar_sync(1, kConsumers);
+  if (tid < 8) {
+    float v = 1.f;
+    if (MODE != MODE_PLAIN && gam != nullptr && tid < a.batch) {
+      float t = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w) t += red[w][tid];
+      v = rsqrtf(t / (float)a.d_in + a.eps);
+    }
+    inv_rms[tid] = v;
+  }
+
+  // ldmatrix.x4 addressing: lane supplies row (lane&7) + 8*((lane>>3)&1) and
+  // column offset 8*(lane>>4) within a 16-column k-step.
+  const int a_row = (lane & 7) + 8 * ((lane >> 3) & 1);
+  const uint32_t a_lane_off = (uint32_t)(a_row * kMmaSlot + (8 * (lane >> 4)) * 2);
+  const int bn = lane >> 2;                  // B column (batch row) held by this lane
+  const bool b_ok = bn < a.batch;
+  const uint16_t* xh = xs_hi + (size_t)(b_ok ? bn : 0) * a.d_in + 2 * (lane & 3);
+  const uint16_t* xl = xs_lo + (size_t)(b_ok ? bn : 0) * a.d_in + 2 * (lane & 3);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+
+  for (int j = 0; j < total; ++j) {
+    const int s = j % a.nstages;
+    const int mt = j / a.nchunks, c = j - mt * a.nchunks;
+    const int col0 = c * kMmaKC;
+    const int seg = min(kMmaKC, a.d_in - col0);
+    if (!mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull)) return;
+    const uint32_t stage = smem_u32(ring + (size_t)s * kMmaStage) + a_lane_off;
+#pragma unroll 4
+    for (int kk = 0; kk < 16; ++kk) {
+      const int k = warp * 256 + kk * 16;
+      if (k < seg) {
+        uint32_t af[4];
+        ldsm_x4(stage + k * 2, af);
+        uint32_t b0 = 0u, b1 = 0u;
+        if (b_ok) {
+          b0 = *reinterpret_cast<const uint32_t*>(xh + col0 + k);
+          b1 = *reinterpret_cast<const uint32_t*>(xh + col0 + k + 8);
+        }
+        Mma<T>::run(acc, af[0], af[1], af[2], af[3], b0, b1);
+        if constexpr (SPLIT) {
+          uint32_t l0 = 0u, l1 = 0u;
+          if (b_ok) {
+            l0 = *reinterpret_cast<const uint32_t*>(xl + col0 + k);
+            l1 = *reinterpret_cast<const uint32_t*>(xl + col0 + k + 8);
+          }
+          Mma<T>::run(acc, af[0], af[1], af[2], af[3], l0, l1);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (c == a.nchunks - 1) {
+      // m-tile done: accumulator rows (lane>>2) and (lane>>2)+8, columns 2*(lane&3) + {0,1}
+      const int r = mt * 16 + (lane >> 2), n0 = 2 * (lane & 3);
+      float* pw = part + (size_t)warp * nmt_max * 16 * a.batch;
+      if (n0 < a.batch) {
+        pw[(size_t)r * a.batch + n0] = acc[0];
+        pw[(size_t)(r + 8) * a.batch + n0] = acc[2];
+      }
+      if (n0 + 1 < a.batch) {
+        pw[(size_t)r * a.batch + n0 + 1] = acc[1];
+        pw[(size_t)(r + 8) * a.batch + n0 + 1] = acc[3];
+      }
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    }
+  }
+  named_bar_sync(1, kConsumers);
+
+  T* y = static_cast<T*>(a.y);
+  const T* res = static_cast<const T*>(a.residual);
+  for (int idx = tid; idx < nrows * a.batch; idx += kConsumers) {
+    const int b = idx / nrows, r = idx - b * nrows;
+    const int mt = r / RPT, q = r - mt * RPT;
+    auto sum_row = [&](int slot) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w)
+        t += part[((size_t)w * nmt_max * 16 + mt * 16 + slot) * a.batch + b];
+      return t;
+    };
+    float v;
+    if constexpr (MODE == MODE_SWIGLU) {
+      const float sc = inv_rms[b];
+      v = silu(sum_row(q) * sc) * (sum_row(8 + q) * sc);
+    } else if constexpr (MODE == MODE_NORM) {
+      v = sum_row(q) * inv_rms[b];
+    } else {
+      v = sum_row(q);
+    }
+    const size_t o = (size_t)b * a.d_out + row0 + r;
+    if (res != nullptr) v += Elem<T>::to_f(res[o]);
+    y[o] = Elem<T>::from_f(v);
+  }
+}
+
+// Shared-memory bytes of the tensor-core variant for a stage count (0 if it
+// cannot run: d_in % 16 != 0 or batch > 8).
+size_t mma_smem_bytes(const GemvArgs& a, int rpt, int nst) {
+  if (a.d_in % 16 != 0 || a.batch > 8) return 0;
+  const int nmt_max = (a.max_rows + rpt - 1) / rpt;
+  return (size_t)nst * (kMmaStage + 16) + (size_t)kConsumerWarps * nmt_max * 16 * a.batch * 4 +
+         (size_t)a.batch * a.d_in * 4 + 256;
+}
+
+template <typename T, int MODE>
+int launch_mma(GemvArgs a, cudaStream_t st, const DeviceInfo& dev, size_t smem) {
+  a.kc = kMmaKC;
+  a.nchunks = (a.d_in + kMmaKC - 1) / kMmaKC;
+  const void* kern = (a.gamma != nullptr)   // x alone is exact in 16 bits: no low part
+                         ? reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, true>)
+                         : reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, false>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return (int)e;
+  return launch_pdl(kern, dim3(a.d_out < dev.num_sms ? a.d_out : dev.num_sms), dim3(kThreads),
+                    smem, st, &a);
+}
+
 template <typename T, int NB, int MODE>
 int launch_nb(GemvArgs a, cudaStream_t st, const DeviceInfo& dev) {
   constexpr int KCG = (NB >= 8) ? 1 : 8 / NB;    // x registers: NB * KCG * 8 = 64
@@ -281,7 +527,24 @@ int launch_nb(GemvArgs a, cudaStream_t st, const DeviceInfo& dev) {
 }
 
 template <typename T, int MODE>
-int launch_t(const GemvArgs& a, cudaStream_t st, const DeviceInfo& dev) {
+int launch_t(const GemvArgs& a0, cudaStream_t st, const DeviceInfo& dev) {
+  static const bool simt_only = [] {
+    const char* v = std::getenv("DBK_GEMV_SIMT");
+    return v && v[0] == '1';
+  }();
+  GemvArgs a = a0;
+  {
+    const int grid = a.d_out < dev.num_sms ? a.d_out : dev.num_sms;
+    a.max_rows = (a.d_out + grid - 1) / grid;
+    const int rpt = (MODE == MODE_SWIGLU) ? 8 : 16;
+    for (int nst = kMmaStages; nst >= 2 && !simt_only; --nst) {
+      const size_t smem = mma_smem_bytes(a, rpt, nst);
+      if (smem != 0 && smem <= (size_t)dev.max_smem_optin - 1024) {
+        a.nstages = nst;
+        return launch_mma<T, MODE>(a, st, dev, smem);
+      }
+    }
+  }
   if (a.batch <= 1) return launch_nb<T, 1, MODE>(a, st, dev);
   if (a.batch <= 2) return launch_nb<T, 2, MODE>(a, st, dev);
   if (a.batch <= 4) return launch_nb<T, 4, MODE>(a, st, dev);
