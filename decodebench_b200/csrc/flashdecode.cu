@@ -18,14 +18,18 @@
 //   * A producer warp streams K and V tiles into a ring of 32 KB stages tracked
 //     by mbarriers, gathering a paged cache ([page, kv_head, page_size, 128],
 //     per-head page blocks contiguous) through the int32 page table.
-//   * G <= 2 (MHA-like): cp.async.bulk row runs; eight consumer warps each take
-//     8 tokens of a tile with their own online-softmax state on CUDA cores.
-//   * G >= 4 (GQA): the G query heads of a kv head form the M=16 rows of
+//   * Tensor-core path (any G, whenever 16-token boxes stay inside pages): the
+//     G query heads of a kv head form the first G of the M=16 rows of
 //     mma.m16n8k16 tiles. K/V arrive by tiled TMA (cp.async.bulk.tensor) with a
 //     128-byte swizzle so ldmatrix reads are conflict free; two groups of four
 //     warps take alternate stages, each warp 16 tokens: S = Q K^T (fp32
 //     accumulate), online softmax in registers, O += P V with P split into a
 //     high and a low 16-bit part so the probabilities keep fp32-like accuracy.
+//     (On CUDA cores the 16-bit -> fp32 conversions of K and V alone cap the
+//     rate near half of HBM bandwidth; the tensor cores take them for free.)
+//   * CUDA-core path (G <= 2 with page sizes that are not multiples of 16):
+//     cp.async.bulk page runs; eight consumer warps each take 8 tokens of a tile
+//     with their own online-softmax state.
 #include <mutex>
 #include <type_traits>
 
@@ -140,9 +144,8 @@ __device__ __forceinline__ int range_start(int64_t c, int64_t T, int64_t grid) {
 }
 
 // ------------------------------------------------------------------ kernel
-template <typename T, int G>
+template <typename T, int G, bool kMma>
 __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_constant__ FdArgs a) {
-  constexpr bool kMma = (G >= 4);
   constexpr int kHalf = kTile * 64 * (int)sizeof(T);        // 64 tokens x 64 dims (8 KB)
   constexpr int kStage = 2 * kTile * kD * (int)sizeof(T);   // K tile | V tile (32 KB)
   extern __shared__ uint8_t smem_raw[];
@@ -187,34 +190,28 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
 
   if (warp == kWarps) {
     // ------------------------------------------------------------ producer
-    if (lane != 0) return;
+    // The whole warp gathers: for each group of 32 tiles, lane l looks up the
+    // cache rows of tile (group + l) in parallel (one page-table latency per
+    // 32 tiles instead of one per box); lane 0 then issues the copies in order.
     const uint64_t pol = policy_evict_first();
-    if constexpr (kMma) { prefetch_tmap(&a.kmap); prefetch_tmap(&a.vmap); }
-    TileWalker w(a, tile0, u0);
-    for (int u = u0, j = 0; u < u1; ++u, ++j, w.next()) {
-      const int s = j % a.nstages;
-      if (j >= a.nstages && !mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty))
-        return;
-      const int n = w.ntok();
-      uint8_t* dk = smem + (size_t)s * kStage;
-      uint8_t* dv = dk + kStage / 2;
-      if constexpr (kMma) {
-        // boxes of 16 tokens x 64 dims; both dim halves of K and of V
-        int boxes = 0;
-        for (int t = 0; t < n; t += kBoxRows) ++boxes;
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(boxes * 4 * kBoxRows * 128));
-        for (int t = 0; t < n; t += kBoxRows) {
-          int run;
-          const int64_t r = kv_rowidx(a, w.b, w.hk, w.tt * kTile + t, &run);
-          for (int h = 0; h < 2; ++h) {
-            tma_load_2d(dk + h * kHalf + t * 128, &a.kmap, h * 64, (int)r, &full[s], pol);
-            tma_load_2d(dv + h * kHalf + t * 128, &a.vmap, h * 64, (int)r, &full[s], pol);
-          }
-        }
-      } else {
+    if constexpr (kMma) {
+      if (lane == 0) { prefetch_tmap(&a.kmap); prefetch_tmap(&a.vmap); }
+    }
+    const T* K = static_cast<const T*>(a.k);
+    const T* V = static_cast<const T*>(a.v);
+    const bool boxed = (a.pages == nullptr) || (a.page_size % kBoxRows == 0);
+    if (!boxed) {
+      // page_size not a multiple of 16 (CUDA-core path only): page runs one by one
+      if (lane != 0) return;
+      TileWalker w(a, tile0, u0);
+      for (int u = u0, j = 0; u < u1; ++u, ++j, w.next()) {
+        const int s = j % a.nstages;
+        if (j >= a.nstages && !mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty))
+          return;
+        const int n = w.ntok();
+        uint8_t* dk = smem + (size_t)s * kStage;
+        uint8_t* dv = dk + kStage / 2;
         mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * n * kD * sizeof(T)));
-        const T* K = static_cast<const T*>(a.k);
-        const T* V = static_cast<const T*>(a.v);
         for (int t = 0; t < n;) {
           int run;
           const int64_t r = kv_rowidx(a, w.b, w.hk, w.tt * kTile + t, &run);
@@ -225,6 +222,66 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
           t += m;
         }
       }
+      return;
+    }
+    TileWalker w(a, tile0, min(u0 + lane, u1 - 1));
+    for (int g0 = u0; g0 < u1; g0 += 32) {
+      // this lane's tile: g0 + lane
+      int n_l = 0;
+      int64_t r_l[4] = {0, 0, 0, 0};
+      if (g0 + lane < u1) {
+        n_l = w.ntok();
+#pragma unroll
+        for (int bx = 0; bx < 4; ++bx) {
+          int run;
+          if (bx * kBoxRows < n_l) r_l[bx] = kv_rowidx(a, w.b, w.hk, w.tt * kTile + bx * kBoxRows, &run);
+        }
+      }
+      const int cnt = min(32, u1 - g0);
+      bool gave_up = false;
+      for (int i = 0; i < cnt; ++i) {
+        const int n = __shfl_sync(0xffffffffu, n_l, i);
+        int64_t r[4];
+#pragma unroll
+        for (int bx = 0; bx < 4; ++bx) r[bx] = __shfl_sync(0xffffffffu, r_l[bx], i);
+        if (lane == 0 && !gave_up) {
+          const int j = g0 - u0 + i;
+          const int s = j % a.nstages;
+          if (j >= a.nstages &&
+              !mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty))
+            gave_up = true;   // the error is recorded; leave after this group
+          else {
+            uint8_t* dk = smem + (size_t)s * kStage;
+            uint8_t* dv = dk + kStage / 2;
+            const int boxes = (n + kBoxRows - 1) / kBoxRows;
+            if constexpr (kMma) {
+              // boxes of 16 tokens x 64 dims; both dim halves of K and of V
+              mbar_arrive_expect_tx(&full[s], (uint32_t)(boxes * 4 * kBoxRows * 128));
+#pragma unroll
+              for (int bx = 0; bx < 4; ++bx)
+                for (int h = 0; h < 2 && bx < boxes; ++h) {
+                  tma_load_2d(dk + h * kHalf + bx * kBoxRows * 128, &a.kmap, h * 64, (int)r[bx],
+                              &full[s], pol);
+                  tma_load_2d(dv + h * kHalf + bx * kBoxRows * 128, &a.vmap, h * 64, (int)r[bx],
+                              &full[s], pol);
+                }
+            } else {
+              mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * n * kD * sizeof(T)));
+#pragma unroll
+              for (int bx = 0; bx < 4; ++bx) {
+                if (bx >= boxes) break;
+                const int m = min(kBoxRows, n - bx * kBoxRows);
+                const uint32_t bytes = (uint32_t)(m * kD * sizeof(T));
+                const size_t so = (size_t)bx * kBoxRows * kD * sizeof(T);
+                bulk_g2s(dk + so, K + r[bx] * kD, bytes, &full[s], pol);
+                bulk_g2s(dv + so, V + r[bx] * kD, bytes, &full[s], pol);
+              }
+            }
+          }
+        }
+      }
+      if (__shfl_sync(0xffffffffu, gave_up ? 1 : 0, 0)) return;
+      for (int k = 0; k < 32; ++k) w.next();
     }
     return;
   }
@@ -529,7 +586,7 @@ size_t ws_bytes_for(int grid, int batch, int hq, int hkv) {
 }
 
 template <typename T, int G>
-int launch_g(FdArgs a, cudaStream_t st, const DeviceInfo& dev, int grid) {
+int launch_g(FdArgs a, cudaStream_t st, const DeviceInfo& dev, int grid, bool mma) {
   constexpr int kStage = 2 * kTile * kD * (int)sizeof(T);
   const size_t fixed = 1024 + (size_t)kWarps * G * kMrg * 4 + (size_t)(a.batch + 1) * 4 + 64;
   int nst = kMaxStages;
@@ -537,19 +594,19 @@ int launch_g(FdArgs a, cudaStream_t st, const DeviceInfo& dev, int grid) {
   a.nstages = nst;
   const size_t smem = (size_t)nst * (kStage + 16) + fixed;
   if (smem > (size_t)dev.max_smem_optin) return DBK_ESHAPE;
-  auto kern = flashdecode_kernel<T, G>;
+  auto kern = mma ? flashdecode_kernel<T, G, true> : flashdecode_kernel<T, G, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
   return launch_pdl(reinterpret_cast<const void*>(kern), dim3(grid), dim3(kThreads), smem, st, &a);
 }
 
 template <typename T>
-int launch_t(const FdArgs& a, int G, cudaStream_t st, const DeviceInfo& dev, int grid) {
+int launch_t(const FdArgs& a, int G, cudaStream_t st, const DeviceInfo& dev, int grid, bool mma) {
   switch (G) {
-    case 1: return launch_g<T, 1>(a, st, dev, grid);
-    case 2: return launch_g<T, 2>(a, st, dev, grid);
-    case 4: return launch_g<T, 4>(a, st, dev, grid);
-    case 8: return launch_g<T, 8>(a, st, dev, grid);
+    case 1: return launch_g<T, 1>(a, st, dev, grid, mma);
+    case 2: return launch_g<T, 2>(a, st, dev, grid, mma);
+    case 4: return launch_g<T, 4>(a, st, dev, grid, mma);
+    case 8: return launch_g<T, 8>(a, st, dev, grid, mma);
     default: return DBK_ESHAPE;
   }
 }
@@ -615,7 +672,10 @@ extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v
   a.page_size = page_table ? page_size : max_len;
   a.max_pages = page_table ? max_pages_per_seq : 1;
   a.qscale = scale * kLog2e;
-  if (G >= 4) {
+  // Tensor-core path whenever 16-token TMA boxes stay inside pages; CUDA cores
+  // otherwise (page sizes that are not multiples of 16, G <= 2 only).
+  const bool mma = (page_table == nullptr) || (page_size % kBoxRows == 0);
+  if (mma) {
     // 2-D views [rows, 128] of the caches for the tensor-core path's TMA boxes.
     // Contiguous caches: exact extent, so a box overhanging the end of the cache
     // reads zeros. Paged caches: the page count is not an argument; every box
@@ -629,8 +689,8 @@ extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v
     if (rc) return rc;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return dtype == DBK_F16 ? launch_t<__half>(a, G, st, dev, grid)
-                          : launch_t<__nv_bfloat16>(a, G, st, dev, grid);
+  return dtype == DBK_F16 ? launch_t<__half>(a, G, st, dev, grid, mma)
+                          : launch_t<__nv_bfloat16>(a, G, st, dev, grid, mma);
 }
 
 // ---------------------------------------------------------------------------

@@ -116,6 +116,8 @@ FD_CASES = [
     (2, 8, 4, 512, [300, 0], 0, 64, BF16),                 # empty sequence
     (4, 8, 2, 1024, [1024, 1, 513, 777], 128, 0, F16),     # G=4
     (2, 64, 8, 4096, [4096, 2500], 64, 0, BF16),           # C5 head layout
+    (2, 4, 2, 300, [300, 77], 20, 0, F16),                 # page size not a multiple of 16:
+    (2, 2, 2, 300, [1, 299], 12, 0, BF16),                 #   CUDA-core path
 ]
 
 
