@@ -84,6 +84,21 @@ int encode_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t inner
   return r == CUDA_SUCCESS ? DBK_OK : DBK_ESHAPE;
 }
 
+int encode_tmap_kv3d(CUtensorMap* out, const void* base, int dtype, uint64_t rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return (int)cudaErrorNotSupported;
+  if (!aligned16(base)) return DBK_EALIGN;
+  const cuuint64_t dims[3] = {64, 2, rows};
+  const cuuint64_t strides[2] = {128, 256};
+  const cuuint32_t box[3] = {64, 2, 16};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(out, dtype == DBK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                  3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DBK_OK : DBK_ESHAPE;
+}
+
 int launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                void* args) {
   cudaLaunchConfig_t cfg{};

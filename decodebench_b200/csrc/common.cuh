@@ -116,6 +116,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 
+// Tiled 3-D TMA load (no multicast) at coordinates (x, y, z).
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;"
+      ::"r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

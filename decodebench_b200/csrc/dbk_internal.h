@@ -33,6 +33,12 @@ int encode_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t inner
                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
                    bool swizzle128);
 
+// 3-D tiled TMA descriptor viewing a row-major [rows, 128] matrix of 16-bit
+// elements as [rows][2 halves][64]: one box (16 rows x both halves) reads 16
+// whole 256-byte rows (4 KB contiguous) and lands as 32 swizzled 128-byte lines,
+// line = 2 * row + half.
+int encode_tmap_kv3d(CUtensorMap* out, const void* base, int dtype, uint64_t rows);
+
 // Launch `func(*args)` (one by-value struct parameter) with programmatic
 // dependent launch enabled unless DBK_PDL=0 is set in the environment.
 int launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,

@@ -20,8 +20,9 @@
 //     per-head page blocks contiguous) through the int32 page table.
 //   * Tensor-core path (any G, whenever 16-token boxes stay inside pages): the
 //     G query heads of a kv head form the first G of the M=16 rows of
-//     mma.m16n8k16 tiles. K/V arrive by tiled TMA (cp.async.bulk.tensor) with a
-//     128-byte swizzle so ldmatrix reads are conflict free; two groups of four
+//     mma.m16n8k16 tiles. K/V arrive by tiled TMA (cp.async.bulk.tensor over a
+//     3-D view [rows][2][64], so each box reads 16 whole rows = 4 KB contiguous)
+//     with a 128-byte swizzle so ldmatrix reads are conflict free; two groups of four
 //     warps take alternate stages, each warp 16 tokens: S = Q K^T (fp32
 //     accumulate), online softmax in registers, O += P V with P split into a
 //     high and a low 16-bit part so the probabilities keep fp32-like accuracy.
@@ -146,7 +147,6 @@ __device__ __forceinline__ int range_start(int64_t c, int64_t T, int64_t grid) {
 // ------------------------------------------------------------------ kernel
 template <typename T, int G, bool kMma>
 __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_constant__ FdArgs a) {
-  constexpr int kHalf = kTile * 64 * (int)sizeof(T);        // 64 tokens x 64 dims (8 KB)
   constexpr int kStage = 2 * kTile * kD * (int)sizeof(T);   // K tile | V tile (32 KB)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -258,13 +258,11 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
               // boxes of 16 tokens x 64 dims; both dim halves of K and of V
               mbar_arrive_expect_tx(&full[s], (uint32_t)(boxes * 4 * kBoxRows * 128));
 #pragma unroll
-              for (int bx = 0; bx < 4; ++bx)
-                for (int h = 0; h < 2 && bx < boxes; ++h) {
-                  tma_load_2d(dk + h * kHalf + bx * kBoxRows * 128, &a.kmap, h * 64, (int)r[bx],
-                              &full[s], pol);
-                  tma_load_2d(dv + h * kHalf + bx * kBoxRows * 128, &a.vmap, h * 64, (int)r[bx],
-                              &full[s], pol);
-                }
+              for (int bx = 0; bx < 4; ++bx) {
+                if (bx >= boxes) break;
+                tma_load_3d(dk + bx * kBoxRows * 256, &a.kmap, 0, 0, (int)r[bx], &full[s], pol);
+                tma_load_3d(dv + bx * kBoxRows * 256, &a.vmap, 0, 0, (int)r[bx], &full[s], pol);
+              }
             } else {
               mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * n * kD * sizeof(T)));
 #pragma unroll
@@ -350,9 +348,8 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             // ragged tail: zero this warp's V rows >= n (their probabilities are 0,
             // but the rows may hold stale or out-of-sequence data)
             for (int r = max(n, t0); r < t0 + 16; ++r) {
-              uint8_t* p0 = smem + (size_t)s * kStage + kStage / 2 + r * 128;
-              reinterpret_cast<uint4*>(p0)[lane & 7] = make_uint4(0, 0, 0, 0);
-              reinterpret_cast<uint4*>(p0 + kHalf)[lane & 7] = make_uint4(0, 0, 0, 0);
+              uint8_t* p0 = smem + (size_t)s * kStage + kStage / 2 + r * 256;
+              reinterpret_cast<uint4*>(p0)[lane & 15] = make_uint4(0, 0, 0, 0);
             }
             fence_proxy_async_smem();   // order these writes before the next TMA refill
             __syncwarp();
@@ -368,7 +365,8 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
               const int chunk = kp * 4 + (lane >> 3);     // 16-byte chunk of the 256-byte row
               const int h = chunk >> 3, c = chunk & 7;
               uint32_t kb[4];
-              ldsm_x4(kst + h * kHalf + tok * 128 + ((c ^ (tok & 7)) << 4), kb);
+              const int line = 2 * tok + h;
+              ldsm_x4(kst + line * 128 + ((c ^ (line & 7)) << 4), kb);
               Mma<T>::run(sc[nt], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, kb[0], kb[1]);
               Mma<T>::run(sc[nt], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, kb[2], kb[3]);
             }
@@ -415,7 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             const int chunk = np * 2 + (lane >> 4);
             const int h = chunk >> 3, c = chunk & 7;
             uint32_t vb[4];
-            ldsm_x4_t(vst + h * kHalf + tok * 128 + ((c ^ (tok & 7)) << 4), vb);
+            const int line = 2 * tok + h;
+            ldsm_x4_t(vst + line * 128 + ((c ^ (line & 7)) << 4), vb);
             float d0[4] = {o[4 * np], o[4 * np + 1], 0.f, 0.f};
             float d1[4] = {o[4 * np + 2], o[4 * np + 3], 0.f, 0.f};
             Mma<T>::run(d0, ph0, 0u, ph2, 0u, vb[0], vb[1]);
@@ -683,9 +682,9 @@ extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v
     // one page of the table, so the view's extent only needs to cover them.
     const uint64_t prow = page_table ? (((uint64_t)1 << 31) - 1)
                                      : (uint64_t)batch * n_kv_heads * max_len;
-    rc = encode_tmap_2d(&a.kmap, k_cache, dtype, kD, prow, kD * 2, 64, kBoxRows, true);
+    rc = encode_tmap_kv3d(&a.kmap, k_cache, dtype, prow);
     if (rc) return rc;
-    rc = encode_tmap_2d(&a.vmap, v_cache, dtype, kD, prow, kD * 2, 64, kBoxRows, true);
+    rc = encode_tmap_kv3d(&a.vmap, v_cache, dtype, prow);
     if (rc) return rc;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
