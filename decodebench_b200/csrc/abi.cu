@@ -88,9 +88,9 @@ int encode_tmap_kv3d(CUtensorMap* out, const void* base, int dtype, uint64_t row
   EncodeTiledFn fn = encode_fn();
   if (!fn) return (int)cudaErrorNotSupported;
   if (!aligned16(base)) return DBK_EALIGN;
-  const cuuint64_t dims[3] = {64, 2, rows};
-  const cuuint64_t strides[2] = {128, 256};
-  const cuuint32_t box[3] = {64, 2, 16};
+  const cuuint64_t dims[3] = {64, rows, 2};
+  const cuuint64_t strides[2] = {256, 128};
+  const cuuint32_t box[3] = {64, 16, 2};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(out, dtype == DBK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                   3, const_cast<void*>(base), dims, strides, box, estr,

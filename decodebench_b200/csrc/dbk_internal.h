@@ -34,9 +34,10 @@ int encode_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t inner
                    bool swizzle128);
 
 // 3-D tiled TMA descriptor viewing a row-major [rows, 128] matrix of 16-bit
-// elements as [rows][2 halves][64]: one box (16 rows x both halves) reads 16
-// whole 256-byte rows (4 KB contiguous) and lands as 32 swizzled 128-byte lines,
-// line = 2 * row + half.
+// elements as [2 halves][rows][64] (strides 128 B and 256 B): one box (16 rows x
+// both halves) reads 16 whole 256-byte rows (4 KB) and lands as 32 swizzled
+// 128-byte lines, line = 16 * half + row, so 8 consecutive rows of one half
+// occupy 8 different swizzle phases (conflict-free ldmatrix).
 int encode_tmap_kv3d(CUtensorMap* out, const void* base, int dtype, uint64_t rows);
 
 // Launch `func(*args)` (one by-value struct parameter) with programmatic

@@ -21,7 +21,7 @@
 //   * Tensor-core path (any G, whenever 16-token boxes stay inside pages): the
 //     G query heads of a kv head form the first G of the M=16 rows of
 //     mma.m16n8k16 tiles. K/V arrive by tiled TMA (cp.async.bulk.tensor over a
-//     3-D view [rows][2][64], so each box reads 16 whole rows = 4 KB contiguous)
+//     3-D view [2][rows][64], so each box reads 16 whole rows = 4 KB)
 //     with a 128-byte swizzle so ldmatrix reads are conflict free; two groups of four
 //     warps take alternate stages, each warp 16 tokens: S = Q K^T (fp32
 //     accumulate), online softmax in registers, O += P V with P split into a
@@ -260,8 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
 #pragma unroll
               for (int bx = 0; bx < 4; ++bx) {
                 if (bx >= boxes) break;
-                tma_load_3d(dk + bx * kBoxRows * 256, &a.kmap, 0, 0, (int)r[bx], &full[s], pol);
-                tma_load_3d(dv + bx * kBoxRows * 256, &a.vmap, 0, 0, (int)r[bx], &full[s], pol);
+                tma_load_3d(dk + bx * kBoxRows * 256, &a.kmap, 0, (int)r[bx], 0, &full[s], pol);
+                tma_load_3d(dv + bx * kBoxRows * 256, &a.vmap, 0, (int)r[bx], 0, &full[s], pol);
               }
             } else {
               mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * n * kD * sizeof(T)));
@@ -348,8 +348,9 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             // ragged tail: zero this warp's V rows >= n (their probabilities are 0,
             // but the rows may hold stale or out-of-sequence data)
             for (int r = max(n, t0); r < t0 + 16; ++r) {
-              uint8_t* p0 = smem + (size_t)s * kStage + kStage / 2 + r * 256;
-              reinterpret_cast<uint4*>(p0)[lane & 15] = make_uint4(0, 0, 0, 0);
+              uint8_t* p0 = smem + (size_t)s * kStage + kStage / 2 +
+                            ((r >> 4) * 32 + (lane >> 4) * 16 + (r & 15)) * 128;
+              reinterpret_cast<uint4*>(p0)[lane & 7] = make_uint4(0, 0, 0, 0);
             }
             fence_proxy_async_smem();   // order these writes before the next TMA refill
             __syncwarp();
@@ -365,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
               const int chunk = kp * 4 + (lane >> 3);     // 16-byte chunk of the 256-byte row
               const int h = chunk >> 3, c = chunk & 7;
               uint32_t kb[4];
-              const int line = 2 * tok + h;
+              const int line = (tok >> 4) * 32 + h * 16 + (tok & 15);
               ldsm_x4(kst + line * 128 + ((c ^ (line & 7)) << 4), kb);
               Mma<T>::run(sc[nt], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, kb[0], kb[1]);
               Mma<T>::run(sc[nt], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, kb[2], kb[3]);
@@ -413,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             const int chunk = np * 2 + (lane >> 4);
             const int h = chunk >> 3, c = chunk & 7;
             uint32_t vb[4];
-            const int line = 2 * tok + h;
+            const int line = (tok >> 4) * 32 + h * 16 + (tok & 15);
             ldsm_x4_t(vst + line * 128 + ((c ^ (line & 7)) << 4), vb);
             float d0[4] = {o[4 * np], o[4 * np + 1], 0.f, 0.f};
             float d1[4] = {o[4 * np + 2], o[4 * np + 3], 0.f, 0.f};
