@@ -10,6 +10,9 @@
 namespace dbk {
 
 __device__ int dbk_device_error = 0;
+#ifdef DBK_TRACE
+__device__ unsigned long long dbk_trace[2048 * 16];
+#endif
 
 namespace {
 constexpr int kMaxDevices = 64;

@@ -41,6 +41,25 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---------------------------------------------------------------- dev tracing
+// Phase timestamps for development builds (-DDBK_TRACE) only; compiled out of
+// the library. Slot k of CTA c is written to dbk_trace[c * 16 + k].
+#ifdef DBK_TRACE
+extern __device__ unsigned long long dbk_trace[2048 * 16];
+#define DBK_MARK(cond, slot)                                              \
+  do {                                                                    \
+    if (cond) {                                                           \
+      unsigned long long t_;                                              \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));              \
+      dbk::dbk_trace[blockIdx.x * 16 + (slot)] = t_;                      \
+    }                                                                     \
+  } while (0)
+#else
+#define DBK_MARK(cond, slot) \
+  do {                       \
+  } while (0)
+#endif
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
@@ -139,6 +158,14 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
 __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+
+// Transpose an 8x8 matrix of 16-bit values held as one register per thread
+// (thread t: row t/4, columns 2*(t%4) and 2*(t%4)+1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
 }
 
 template <typename T> struct Mma;

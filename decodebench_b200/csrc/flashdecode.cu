@@ -157,6 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
   __shared__ int s_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  DBK_MARK(tid == 0, 0);
   if (tid == 0) {
     // A stage is released by every consumer warp (CUDA-core path) or by the
     // four warps of the group that consumed it (tensor-core path).
@@ -168,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
   }
   if (warp == 0) build_tile_offsets(a, tile0, lane);
   __syncthreads();
+  DBK_MARK(tid == 0, 1);
   asm volatile("griddepcontrol.launch_dependents;");
 
   // Sequences of length 0 have no tiles: their output is defined as zeros.
@@ -280,25 +282,28 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
       }
       if (__shfl_sync(0xffffffffu, gave_up ? 1 : 0, 0)) return;
       for (int k = 0; k < 32; ++k) w.next();
+      DBK_MARK(lane == 0 && g0 == u0, 8);
     }
+    DBK_MARK(lane == 0, 9);
     return;
   }
 
   // -------------------------------------------------------------- consumers
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  DBK_MARK(tid == 0, 2);
   const T* q = static_cast<const T*>(a.q);
   T* out = static_cast<T*>(a.out);
 
   // Per-warp online-softmax state. CUDA-core path: lane owns dims 4l..4l+3 of
-  // each of the G heads. Tensor-core path: lane owns head r = lane/4 and dims
-  // 8*nd + 2*(lane%4) + {0,1} for nd < 16.
+  // each of the G heads. Tensor-core path: lane owns heads 2*(lane%4) + {0,1}
+  // and dims 16*mt + lane/4 (+8) for mt < 8 (the O^T accumulator fragment).
   constexpr int kO = kMma ? 32 : 4 * G;
-  constexpr int kS = kMma ? 1 : G;
+  constexpr int kS = kMma ? 2 : G;
   float o[kO], m[kS], l[kS];
   float qr[kMma ? 1 : G][4];
-  uint32_t qa[kMma ? 8 : 1][2];     // A fragments of Q (rows 0..7 = heads), 8 k-steps
+  uint32_t qa[kMma ? 8 : 1][2];     // B fragments of Q^T (columns = heads), 8 k-steps
   const int grp = warp >> 2, wi = warp & 3;
-  const int r_head = lane >> 2;     // tensor-core path: this lane's head row
+  const int r_head = lane >> 2;     // tensor-core path: the head whose Q this lane loads
 
   TileWalker w(a, tile0, u0);
   int seg_first = u0;
@@ -320,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             qa[kk][0] = qa[kk][1] = 0u;
           }
         }
-        m[0] = -INFINITY; l[0] = 0.f;
+        m[0] = m[1] = -INFINITY; l[0] = l[1] = 0.f;
 #pragma unroll
         for (int e = 0; e < kO; ++e) o[e] = 0.f;
       } else {
@@ -342,7 +347,13 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
     if constexpr (kMma) {
       if ((j & 1) == grp) {
         if (!mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull)) return;
+        DBK_MARK(lane == 0 && warp == 0 && j == 0, 3);
+        DBK_MARK(lane == 0 && warp == 0 && j == 16, 4);
+#ifdef DBK_FD_SKIP
+        const int t0 = kTile;                   // dev experiment: stream only
+#else
         const int t0 = wi * 16;                 // this warp's 16 tokens
+#endif
         if (t0 < n) {
           if (n < kTile && t0 + 16 > n) {
             // ragged tail: zero this warp's V rows >= n (their probabilities are 0,
@@ -355,77 +366,78 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             fence_proxy_async_smem();   // order these writes before the next TMA refill
             __syncwarp();
           }
-          // S[16 heads x 16 tokens] = Q K^T as two n-tiles of 8 tokens
-          float sc[2][4];
+          // S^T[16 tokens x 8 heads] = K Q^T: tokens are the M rows (no padding);
+          // heads 0..G-1 are the N columns. Two accumulators halve the MMA chain.
+          float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+          {
+            const int tok = t0 + (lane & 7) + 8 * ((lane >> 3) & 1);
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-            const int tok = t0 + nt * 8 + (lane & 7);
-#pragma unroll
-            for (int kp = 0; kp < 4; ++kp) {        // pairs of k-steps: 32 dims
-              const int chunk = kp * 4 + (lane >> 3);     // 16-byte chunk of the 256-byte row
+            for (int kk = 0; kk < 8; ++kk) {
+              const int chunk = 2 * kk + (lane >> 4);     // 16-byte chunk of the 256-byte row
               const int h = chunk >> 3, c = chunk & 7;
-              uint32_t kb[4];
               const int line = (tok >> 4) * 32 + h * 16 + (tok & 15);
-              ldsm_x4(kst + line * 128 + ((c ^ (line & 7)) << 4), kb);
-              Mma<T>::run(sc[nt], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, kb[0], kb[1]);
-              Mma<T>::run(sc[nt], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, kb[2], kb[3]);
+              uint32_t ka[4];
+              ldsm_x4(kst + line * 128 + ((c ^ (line & 7)) << 4), ka);
+              Mma<T>::run((kk & 1) ? sb : sa, ka[0], ka[1], ka[2], ka[3], qa[kk][0], qa[kk][1]);
             }
           }
-          // online softmax on row r_head (fragment elements 0, 1 of each n-tile)
-          float mx = m[0];
+          // fragment: sc[0..1] = tokens t0+g, heads 2q, 2q+1; sc[2..3] = tokens t0+g+8
+          const int g = lane >> 2, qd = lane & 3;
+          float sc[4];
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
+          for (int e = 0; e < 4; ++e) {
+            const int tok = t0 + g + (e >> 1) * 8;
+            sc[e] = (tok < n) ? (sa[e] + sb[e]) * a.qscale : -INFINITY;
+          }
+          // online softmax per head (column): reduce over the 8 lanes sharing qd
+          float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int tok = t0 + nt * 8 + 2 * (lane & 3) + e;
-              const float v = (tok < n) ? sc[nt][e] * a.qscale : -INFINITY;
-              sc[nt][e] = v;
-              mx = fmaxf(mx, v);
-            }
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          const float alpha = exp2f(m[0] - mx);
-          m[0] = mx;
-          float ls = 0.f;
+          for (int o2 = 4; o2 < 32; o2 <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o2));
+          }
+          mx0 = fmaxf(mx0, m[0]);
+          mx1 = fmaxf(mx1, m[1]);
+          const float al0 = exp2f(m[0] - mx0), al1 = exp2f(m[1] - mx1);
+          m[0] = mx0; m[1] = mx1;
+          sc[0] = exp2f(sc[0] - mx0); sc[2] = exp2f(sc[2] - mx0);
+          sc[1] = exp2f(sc[1] - mx1); sc[3] = exp2f(sc[3] - mx1);
+          l[0] = l[0] * al0 + sc[0] + sc[2];      // lane-partial column sums
+          l[1] = l[1] * al1 + sc[1] + sc[3];
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              sc[nt][e] = exp2f(sc[nt][e] - mx);
-              ls += sc[nt][e];
-            }
-          l[0] = l[0] * alpha + ls;             // lane-partial row sum
-#pragma unroll
-          for (int e = 0; e < kO; ++e) o[e] *= alpha;
-          // P as A fragments (rows 8..15 are zero): high and low 16-bit parts
-          const uint32_t ph0 = Mma<T>::pack(sc[0][0], sc[0][1]);
-          const uint32_t ph2 = Mma<T>::pack(sc[1][0], sc[1][1]);
-          uint32_t pl0 = 0u, pl2 = 0u;
+          for (int mt = 0; mt < 8; ++mt) {
+            o[4 * mt] *= al0; o[4 * mt + 2] *= al0;
+            o[4 * mt + 1] *= al1; o[4 * mt + 3] *= al1;
+          }
+          // P^T as the B operand of O^T += V^T P^T: transpose the 8x8 blocks of
+          // the S^T fragment in registers (tokens 0..7 -> b0, 8..15 -> b1), with a
+          // high and a low 16-bit part for bf16.
+          const uint32_t ph0 = movmatrix_trans(Mma<T>::pack(sc[0], sc[1]));
+          const uint32_t ph1 = movmatrix_trans(Mma<T>::pack(sc[2], sc[3]));
+          uint32_t pl0 = 0u, pl1 = 0u;
           if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-            const float2 h0 = Elem<T>::unpack2(ph0), h2 = Elem<T>::unpack2(ph2);
-            pl0 = Mma<T>::pack(sc[0][0] - h0.x, sc[0][1] - h0.y);
-            pl2 = Mma<T>::pack(sc[1][0] - h2.x, sc[1][1] - h2.y);
+            const float2 h0 = Elem<T>::unpack2(Mma<T>::pack(sc[0], sc[1]));
+            const float2 h1 = Elem<T>::unpack2(Mma<T>::pack(sc[2], sc[3]));
+            pl0 = movmatrix_trans(Mma<T>::pack(sc[0] - h0.x, sc[1] - h0.y));
+            pl1 = movmatrix_trans(Mma<T>::pack(sc[2] - h1.x, sc[3] - h1.y));
           }
-          // O[16 x 128] += P[16 x 16 tokens] V[16 tokens x 128]
+          // O^T[128 dims x 8 heads] += V^T[dims x 16 tokens] P^T[16 tokens x 8 heads]
+          {
+            const int tok = t0 + (lane & 7) + 8 * (lane >> 4);
 #pragma unroll
-          for (int np = 0; np < 8; ++np) {          // pairs of 8-dim n-tiles
-            const int tok = t0 + ((lane >> 3) & 1) * 8 + (lane & 7);
-            const int chunk = np * 2 + (lane >> 4);
-            const int h = chunk >> 3, c = chunk & 7;
-            uint32_t vb[4];
-            const int line = (tok >> 4) * 32 + h * 16 + (tok & 15);
-            ldsm_x4_t(vst + line * 128 + ((c ^ (line & 7)) << 4), vb);
-            float d0[4] = {o[4 * np], o[4 * np + 1], 0.f, 0.f};
-            float d1[4] = {o[4 * np + 2], o[4 * np + 3], 0.f, 0.f};
-            Mma<T>::run(d0, ph0, 0u, ph2, 0u, vb[0], vb[1]);
-            Mma<T>::run(d1, ph0, 0u, ph2, 0u, vb[2], vb[3]);
-            if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-              Mma<T>::run(d0, pl0, 0u, pl2, 0u, vb[0], vb[1]);
-              Mma<T>::run(d1, pl0, 0u, pl2, 0u, vb[2], vb[3]);
+            for (int mt = 0; mt < 8; ++mt) {        // 16-dim m-tiles
+              const int chunk = 2 * mt + ((lane >> 3) & 1);
+              const int h = chunk >> 3, c = chunk & 7;
+              const int line = (tok >> 4) * 32 + h * 16 + (tok & 15);
+              uint32_t va[4];
+              ldsm_x4_t(vst + line * 128 + ((c ^ (line & 7)) << 4), va);
+              float* d = &o[4 * mt];
+              float acc4[4] = {d[0], d[1], d[2], d[3]};
+              Mma<T>::run(acc4, va[0], va[1], va[2], va[3], ph0, ph1);
+              if constexpr (std::is_same<T, __nv_bfloat16>::value)
+                Mma<T>::run(acc4, va[0], va[1], va[2], va[3], pl0, pl1);
+              d[0] = acc4[0]; d[1] = acc4[1]; d[2] = acc4[2]; d[3] = acc4[3];
             }
-            o[4 * np] = d0[0]; o[4 * np + 1] = d0[1];
-            o[4 * np + 2] = d1[0]; o[4 * np + 3] = d1[1];
           }
         }
         __syncwarp();
@@ -494,20 +506,27 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
       if (lane == 0) mbar_arrive(&empty[s]);
     }
     if (!seg_end) continue;
+    DBK_MARK(tid == 0, 5);
 
     // ---- segment done: merge the 8 warps' states in shared memory
     named_bar_sync(1, kConsumers);     // readers of the previous segment's mrg are done
     if constexpr (kMma) {
-      float lsum = l[0];
-      lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
-      lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
-      if (r_head < G) {
-        float* dst = mrg + (warp * G + r_head) * kMrg;
+      const int g8 = lane >> 2, qd = lane & 3;
 #pragma unroll
-        for (int nd = 0; nd < 16; ++nd)
-          *reinterpret_cast<float2*>(dst + nd * 8 + 2 * (lane & 3)) =
-              make_float2(o[2 * nd], o[2 * nd + 1]);
-        if ((lane & 3) == 0) { dst[kD] = m[0]; dst[kD + 1] = lsum; }
+      for (int e = 0; e < 2; ++e) {
+        float lsum = l[e];
+#pragma unroll
+        for (int o2 = 4; o2 < 32; o2 <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o2);
+        const int head = 2 * qd + e;
+        if (head < G) {
+          float* dst = mrg + (warp * G + head) * kMrg;
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            dst[16 * mt + g8] = o[4 * mt + e];
+            dst[16 * mt + g8 + 8] = o[4 * mt + 2 + e];
+          }
+          if (g8 == 0) { dst[kD] = m[e]; dst[kD + 1] = lsum; }
+        }
       }
     } else {
 #pragma unroll
@@ -574,7 +593,9 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
       out[((size_t)w.b * a.hq + (size_t)w.hk * G + g) * kD + d] = Elem<T>::from_f(O / L);
     }
     if (tid == 0) a.done[w.row()] = 0;   // ready for the next launch
+    DBK_MARK(tid == 0, 7);
   }
+  DBK_MARK(tid == 0, 6);
 }
 
 size_t ws_bytes_for(int grid, int batch, int hq, int hkv) {
