@@ -31,6 +31,7 @@
 //   * CUDA-core path (G <= 2 with page sizes that are not multiples of 16):
 //     cp.async.bulk page runs; eight consumer warps each take 8 tokens of a tile
 //     with their own online-softmax state.
+#include <cstdlib>
 #include <mutex>
 #include <type_traits>
 
@@ -610,7 +611,12 @@ template <typename T, int G>
 int launch_g(FdArgs a, cudaStream_t st, const DeviceInfo& dev, int grid, bool mma) {
   constexpr int kStage = 2 * kTile * kD * (int)sizeof(T);
   const size_t fixed = 1024 + (size_t)kWarps * G * kMrg * 4 + (size_t)(a.batch + 1) * 4 + 64;
-  int nst = kMaxStages;
+  static const int max_st = [] {   // DBK_FD_STAGES caps the ring depth (tuning knob)
+    const char* v = std::getenv("DBK_FD_STAGES");
+    const int n = v ? std::atoi(v) : kMaxStages;
+    return n < 2 ? 2 : (n > kMaxStages ? kMaxStages : n);
+  }();
+  int nst = max_st;
   while (nst > 2 && (size_t)nst * (kStage + 16) + fixed > (size_t)dev.max_smem_optin - 1024) --nst;
   a.nstages = nst;
   const size_t smem = (size_t)nst * (kStage + 16) + fixed;
