@@ -496,7 +496,113 @@ class GQA(F4):
         return self.costs.flashdecode_bytes([self.cpu_len], 8, 1)
 
 
-WORKLOADS = {"f2": F2, "f1": F1, "f4": F4, "gqa": GQA}
+class MLP(Workload):
+    """Llama-70B-shaped decode MLP, batch 16, d 8192, d_ff 28672,
+    bf16; RMSNorm (eps 1e-5) -> gate/up -> SwiGLU -> down. With N ranks gate/up
+    and down are column-sharded; h is all-gathered between them and y at the end."""
+
+    name = "mlp"
+    kernels_per_step = 3   # prep, gate/up+SwiGLU, down (NCCL kernels at N > 1 not counted)
+
+    def __init__(self, rank, world, torch, batch=16, d=8192, d_ff=28672):
+        from decodebench_b200 import costs, ops
+
+        self.t, self.ops, self.costs = torch, ops, costs
+        self.rank, self.world, self.batch, self.d, self.d_ff = rank, world, batch, d, d_ff
+        self.ff, self.dd = d_ff // world, d // world
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(70 + rank)
+        self.nrep = 1   # 1.41 GB / N per replica, > L2 for N <= 8
+        self.Wg = (torch.randn(self.ff, d, generator=g, device=dev) / math.sqrt(d)).bfloat16()
+        self.Wu = (torch.randn(self.ff, d, generator=g, device=dev) / math.sqrt(d)).bfloat16()
+        self.Wd = (torch.randn(self.dd, d_ff, generator=g, device=dev) / math.sqrt(d_ff)).bfloat16()
+        xg = torch.Generator().manual_seed(42)
+        self.x_cpu = torch.randn(batch, d, generator=xg).bfloat16()
+        self.x = self.x_cpu.to(dev)
+        self.gamma = torch.ones(d, dtype=torch.bfloat16, device=dev)
+        self.h = torch.empty(batch, self.ff, dtype=torch.bfloat16, device=dev)
+        self.h_all = torch.empty(world, batch, self.ff, dtype=torch.bfloat16, device=dev)
+        self.h_full = torch.empty(batch, d_ff, dtype=torch.bfloat16, device=dev)
+        self.y = torch.empty(batch, self.dd, dtype=torch.bfloat16, device=dev)
+        self.y_all = torch.empty(world, batch, self.dd, dtype=torch.bfloat16, device=dev)
+
+    def describe(self):
+        return {"workload": "Llama-70B-shaped decode MLP, batch 16, d 8192, d_ff 28672, bf16: "
+                            "RMSNorm -> gate/up -> SwiGLU -> down (BASELINE config 4)",
+                "global_batch": self.batch, "d_model": self.d, "d_ff": self.d_ff,
+                "parallelism": ("single GPU" if self.world == 1 else
+                                f"tp{self.world}: gate/up and down column-sharded, NCCL "
+                                "all-gather of h and of y"),
+                "l2": "weights 1.41 GB / N per GPU, read once per step (> 126 MB L2)"}
+
+    def step_bytes_total(self):
+        return self.costs.mlp_bytes(self.batch, self.d, self.d_ff)
+
+    def launch_bytes(self):
+        return self.costs.mlp_bytes(self.batch, self.d, self.d_ff) // self.world
+
+    def _gather_h(self):
+        if self.world == 1:
+            return self.h
+        self.t.distributed.all_gather_into_tensor(self.h_all, self.h)
+        # [world, batch, ff] -> [batch, world * ff]
+        self.h_full.copy_(self.h_all.permute(1, 0, 2).reshape(self.batch, self.d_ff))
+        return self.h_full
+
+    def run_kernel(self, rep):
+        self.ops.gateup_swiglu(self.x, self.Wg, self.Wu, gamma=self.gamma, eps=1e-5, out=self.h)
+        self.ops.gemv(self._gather_h(), self.Wd, out=self.y)
+
+    def exchange(self):
+        if self.world > 1:
+            self.t.distributed.all_gather_into_tensor(self.y_all, self.y)
+
+    def e2e_setup(self):
+        t = self.t
+        self.x_host = self.x_cpu.pin_memory()
+        self.out_host = t.empty(self.world * self.y.numel(), dtype=t.bfloat16).pin_memory()
+        self.x_dev = t.empty_like(self.x)
+        return self.x_host.nbytes, self.out_host.nbytes
+
+    def e2e_step(self):
+        self.x_dev.copy_(self.x_host, non_blocking=True)
+        h = self.ops.gateup_swiglu(self.x_dev, self.Wg, self.Wu, gamma=self.gamma, eps=1e-5)
+        if self.world > 1:
+            full = self.t.empty(self.world, *h.shape, dtype=h.dtype, device=h.device)
+            self.t.distributed.all_gather_into_tensor(full, h)
+            h = full.permute(1, 0, 2).reshape(self.batch, self.d_ff)
+        y = self.ops.gemv(h, self.Wd)
+        if self.world > 1:
+            full = self.t.empty(self.world, *y.shape, dtype=y.dtype, device=y.device)
+            self.t.distributed.all_gather_into_tensor(full, y)
+            y = full
+        self.out_host.copy_(y.reshape(-1), non_blocking=True)
+
+    def cpu_setup(self, frac_rows: float = 1.0):
+        import numpy as np
+
+        rng = np.random.default_rng(5)
+        n = max(1, int(self.d_ff * frac_rows))
+        self.cpu_rows = n
+        self.cWg = rng.standard_normal((n, self.d), dtype=np.float32) / math.sqrt(self.d)
+        self.cWu = rng.standard_normal((n, self.d), dtype=np.float32) / math.sqrt(self.d)
+        self.cx = self.x_cpu.float().numpy()
+
+    def cpu_step(self, threads):
+        import numpy as np
+
+        from oracle import oracle as O
+
+        for b in range(self.batch):
+            xn = O.rmsnorm_f32(self.cx[b], np.ones(self.d, np.float32), 1e-5, use_ref=True)
+            O.swiglu_f32(O.ref_gemv_threaded(self.cWg, xn, threads),
+                         O.ref_gemv_threaded(self.cWu, xn, threads), use_ref=True)
+
+    def cpu_step_bytes(self):
+        return 2 * (2 * self.cpu_rows * self.d)
+
+
+WORKLOADS = {"f2": F2, "f1": F1, "f4": F4, "gqa": GQA, "mlp": MLP}
 
 
 # ---------------------------------------------------------------- timing
