@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             }
           }
           // fragment: sc[0..1] = tokens t0+g, heads 2q, 2q+1; sc[2..3] = tokens t0+g+8
-          const int g = lane >> 2, qd = lane & 3;
+          const int g = lane >> 2;
           float sc[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {

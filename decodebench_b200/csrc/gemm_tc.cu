@@ -10,13 +10,20 @@
 // still HBM-bound, but too much work for CUDA cores (~300 us of fp32 FMA vs
 // ~210 us of HBM time), so the contraction runs on the 5th-generation tensor
 // cores while the kernel stays a weight stream:
-//   * D[128 weight rows x N] += A[128 x 64] * B[N x 64]^T per 64-column k-block:
-//     A = a 128-row tile of W, B = the activations (N = batch rounded up to 16);
-//     both K-major, staged by tiled TMA with the 128-byte swizzle, described to
-//     tcgen05.mma by shared-memory descriptors; fp32 accumulators live in TMEM;
-//   * persistent CTAs, one per SM, split the (m-tile, k-block) units evenly
-//     ("stream-K"): CTA c owns units [c*U/G, (c+1)*U/G) in m-major order, so a
-//     CTA's range cuts at most two m-tiles; an m-tile covered by one CTA is
+//   * D[activation rows x 256 weight rows] += A[128 x 16] * B[256 x 16]^T per
+//     16-column k-step: B = a 256-row tile of W, A = the activation rows (R <= 128
+//     real rows; the MMA's 128-row A read runs on into the weight tile that
+//     follows A in shared memory, and those output lanes are never read). A
+//     tcgen05.mma costs ~156 cycles to issue whatever its N (measured), so the
+//     weights take the N = 256 side: 8 KB of weights per instruction keeps the
+//     single issuing thread ahead of HBM, where a 128-row A-side weight tile
+//     (4 KB per instruction) could not keep up. Both operands are K-major,
+//     staged by tiled TMA with the 128-byte swizzle and described to
+//     tcgen05.mma by shared-memory descriptors; fp32 accumulators live in TMEM
+//     (one 256-column accumulator, two for gate and up);
+//   * persistent CTAs, one per SM, split the (n-tile, k-block) units evenly
+//     ("stream-K"): CTA c owns units [c*U/G, (c+1)*U/G) in tile-major order, so
+//     a CTA's range cuts at most two tiles; a tile covered by one CTA is
 //     finished in place, otherwise each contributor writes its fp32 partial to
 //     the workspace and the last to arrive (self-resetting counter) sums the
 //     partials in CTA order (deterministic) and applies the epilogue;
@@ -24,10 +31,11 @@
 //     MMAs (one elected thread; tcgen05.commit releases smem stages), warps 2-5
 //     drain TMEM (tcgen05.ld) and run the epilogue;
 //   * activations that are not exact in 16 bits (x * gamma) are written by a
-//     small prep kernel as a high and a low bf16/fp16 part and both are
-//     multiplied (two MMAs), so the products keep ~16-22 mantissa bits; the prep
-//     kernel also computes inv_rms. Programmatic dependent launch lets the GEMM
-//     start streaming weights while the prep kernel (or the previous op) runs.
+//     small prep kernel as a high and a low bf16/fp16 part, stacked as A rows
+//     (hi rows 0..NB-1, lo rows NB..2NB-1) and summed in the epilogue, so the
+//     products keep ~16-22 mantissa bits at no extra MMA; the prep kernel also
+//     computes inv_rms. Programmatic dependent launch lets the GEMM start
+//     streaming weights while the prep kernel (or the previous op) runs.
 #include <cstdlib>
 #include <cstring>
 #include <type_traits>
@@ -40,23 +48,23 @@ namespace {
 
 enum TcMode : int { TC_PLAIN = 0, TC_NORM = 1, TC_SWIGLU = 2 };
 
-constexpr int kBM = 128;        // weight rows per m-tile
+constexpr int kBN = 256;        // weight rows per tile (the MMA N)
 constexpr int kBK = 64;         // k-block (one 128-byte swizzle atom of 16-bit values)
 constexpr int kTcThreads = 192; // producer, MMA, 4 epilogue warps
-constexpr int kMaxN = 256;
+constexpr int kMaxRows = 128;   // A rows per pass (hi + lo rows when split)
 
 struct TcArgs {
-  CUtensorMap wmap0;   // W (or Wg) [d_out, d_in], box [128 rows x 64]
+  CUtensorMap wmap0;   // W (or Wg) [d_out, d_in], box [256 rows x 64]
   CUtensorMap wmap1;   // Wu for SWIGLU
-  CUtensorMap bmap;    // B operand rows [N, d_in] (x or the prep buffer's hi part), box [N x 64]
-  CUtensorMap bmap_lo; // prep buffer's lo part (SPLIT only)
+  CUtensorMap amap;    // activation rows: x [batch, d_in] or the prep buffer [2 NB, d_in], box [R x 64]
   const void* residual;   // [batch, d_out] or nullptr
   void* y;                // [batch, d_out]
-  const float* inv_rms;   // [N] (NORM / SWIGLU with gamma) or nullptr
-  float* part;            // [2 * grid][NACC][128][N] fp32 partials
-  int* done;              // [m-tiles] arrival counters (zero between launches)
-  int batch, n, d_in, d_out;
-  int mtiles, kblocks;
+  const float* inv_rms;   // [NB] (NORM / SWIGLU with gamma) or nullptr
+  float* part;            // [2 * grid][NACC][batch][256] fp32 partials
+  int* done;              // [n-tiles] arrival counters (zero between launches)
+  int batch, nb, rows;    // batch, its padding to 8 (lo rows start at nb), A rows loaded
+  int d_in, d_out;
+  int ntiles, kblocks;
   int nstages, stage_bytes;
   uint32_t tmem_cols;
 };
@@ -81,14 +89,14 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor: kind::f16, fp32 accumulate, A/B K-major, M = 128.
-__device__ __forceinline__ uint32_t idesc_f16(bool bf16, int n) {
+// Instruction descriptor: kind::f16, fp32 accumulate, A/B K-major, M = 128, N = 256.
+__device__ __forceinline__ uint32_t idesc_f16(bool bf16) {
   uint32_t d = 0;
   d |= 1u << 4;                                      // D format f32
   d |= (bf16 ? 1u : 0u) << 7;                        // A format
   d |= (bf16 ? 1u : 0u) << 10;                       // B format
-  d |= (uint32_t)(n >> 3) << 17;                     // N
-  d |= (uint32_t)(kBM >> 4) << 24;                   // M
+  d |= (uint32_t)(kBN >> 3) << 17;                   // N
+  d |= (uint32_t)(128 >> 4) << 24;                   // M
   return d;
 }
 
@@ -133,6 +141,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) tc_prep_kernel(const T* x, const T* gamma, T* b_hi, T* b_lo,
                                                       float* inv_rms, int batch, int d_in,
                                                       float eps) {
+  // b_hi: rows 0..N-1 of the B buffer; b_lo = b_hi + N * d_in (rows N..2N-1).
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int b = blockIdx.x;
   float ss = 0.f;
@@ -173,24 +182,25 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const T* x, const T* gamma
 // ---------------------------------------------------------------- GEMM kernel
 template <typename T, int MODE, bool SPLIT>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcArgs a) {
-  constexpr int NACC = (MODE == TC_SWIGLU) ? 2 : 1;   // accumulators (gate, up)
-  constexpr int NB = SPLIT ? 2 : 1;                   // B parts (hi, lo)
+  constexpr int NACC = (MODE == TC_SWIGLU) ? 2 : 1;   // output accumulators (gate, up)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.nstages * a.stage_bytes);
   uint64_t* empty = full + a.nstages;
   uint64_t* acc_full = empty + a.nstages;
   uint64_t* acc_empty = acc_full + 1;
+  uint64_t* teardown = acc_empty + 1;
   __shared__ uint32_t s_tmem;
-  __shared__ int s_last[4];
+  __shared__ int s_last;
   __shared__ volatile int s_bail;
+  __shared__ float xbuf[kMaxRows / 2][17];    // lo-row exchange (split)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int N = a.n;
-  const int a_bytes = kBM * kBK * 2;            // 16 KB per A tile
-  const int b_bytes = N * kBK * 2;              // N x 128 B per B tile
+  DBK_MARK(tid == 0, 0);
+  const int a_bytes = a.rows * 128;            // A rows of one k-block
+  const int w_bytes = kBN * 128;               // 32 KB weight tile of one k-block
 
-  const int64_t U = (int64_t)a.mtiles * a.kblocks;
+  const int64_t U = (int64_t)a.ntiles * a.kblocks;
   const int G = (int)min((int64_t)gridDim.x, U);
   if (tid == 0) {
     for (int s = 0; s < a.nstages; ++s) {
@@ -199,6 +209,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 4);
+    mbar_init(teardown, kTcThreads / 32);
     fence_barrier_init();
     s_bail = 0;
   }
@@ -210,6 +221,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  DBK_MARK(tid == 0, 13);
   asm volatile("griddepcontrol.launch_dependents;");
   const uint32_t tmem = s_tmem;
 
@@ -223,43 +235,44 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
       // Weight tiles do not depend on the previous kernel: stream the first
-      // stages' A tiles before waiting for it, their B tiles after.
+      // stages' weights before waiting for it, their activation rows after.
       const int pre = min(a.nstages, u1 - u0);
       for (int j = 0; j < pre; ++j) {
-        const int u = u0 + j, mt = u / a.kblocks, kb = u - mt * a.kblocks;
+        const int u = u0 + j, nt = u / a.kblocks, kb = u - nt * a.kblocks;
         uint8_t* st = smem + (size_t)j * a.stage_bytes;
-        mbar_arrive_expect_tx(&full[j], (uint32_t)(NACC * a_bytes + NB * b_bytes));
-        tma_load_2d(st, &a.wmap0, kb * kBK, mt * kBM, &full[j], pol_w);
-        if constexpr (NACC == 2) tma_load_2d(st + a_bytes, &a.wmap1, kb * kBK, mt * kBM, &full[j], pol_w);
+        mbar_arrive_expect_tx(&full[j], (uint32_t)(a_bytes + NACC * w_bytes));
+        tma_load_2d(st + a_bytes, &a.wmap0, kb * kBK, nt * kBN, &full[j], pol_w);
+        if constexpr (NACC == 2)
+          tma_load_2d(st + a_bytes + w_bytes, &a.wmap1, kb * kBK, nt * kBN, &full[j], pol_w);
       }
+      DBK_MARK(true, 1);
       asm volatile("griddepcontrol.wait;" ::: "memory");
+      DBK_MARK(true, 2);
       for (int j = 0; j < pre; ++j) {
-        const int u = u0 + j, kb = u % a.kblocks;
-        uint8_t* st = smem + (size_t)j * a.stage_bytes + NACC * a_bytes;
-        tma_load_2d(st, &a.bmap, kb * kBK, 0, &full[j], pol_x);
-        if constexpr (SPLIT) tma_load_2d(st + b_bytes, &a.bmap_lo, kb * kBK, 0, &full[j], pol_x);
+        const int kb = (u0 + j) % a.kblocks;
+        tma_load_2d(smem + (size_t)j * a.stage_bytes, &a.amap, kb * kBK, 0, &full[j], pol_x);
       }
       for (int j = pre; j < u1 - u0; ++j) {
         const int s = j % a.nstages;
         if (!mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty)) { s_bail = 1; break; }
-        const int u = u0 + j, mt = u / a.kblocks, kb = u - mt * a.kblocks;
+        const int u = u0 + j, nt = u / a.kblocks, kb = u - nt * a.kblocks;
         uint8_t* st = smem + (size_t)s * a.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(NACC * a_bytes + NB * b_bytes));
-        tma_load_2d(st, &a.wmap0, kb * kBK, mt * kBM, &full[s], pol_w);
-        if constexpr (NACC == 2) tma_load_2d(st + a_bytes, &a.wmap1, kb * kBK, mt * kBM, &full[s], pol_w);
-        tma_load_2d(st + NACC * a_bytes, &a.bmap, kb * kBK, 0, &full[s], pol_x);
-        if constexpr (SPLIT)
-          tma_load_2d(st + NACC * a_bytes + b_bytes, &a.bmap_lo, kb * kBK, 0, &full[s], pol_x);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(a_bytes + NACC * w_bytes));
+        tma_load_2d(st, &a.amap, kb * kBK, 0, &full[s], pol_x);
+        tma_load_2d(st + a_bytes, &a.wmap0, kb * kBK, nt * kBN, &full[s], pol_w);
+        if constexpr (NACC == 2)
+          tma_load_2d(st + a_bytes + w_bytes, &a.wmap1, kb * kBK, nt * kBN, &full[s], pol_w);
       }
+      DBK_MARK(true, 3);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (active) {
-      const uint32_t idesc = idesc_f16(std::is_same<T, __nv_bfloat16>::value, N);
+      const uint32_t idesc = idesc_f16(std::is_same<T, __nv_bfloat16>::value);
       int seg = 0;
       bool first = true;
       for (int j = 0; j < u1 - u0 && !s_bail; ++j) {
-        const int u = u0 + j, mt = u / a.kblocks, kb = u - mt * a.kblocks;
+        const int u = u0 + j, kb = u % a.kblocks;
         const int s = j % a.nstages;
         if (first && seg > 0) {
           // the epilogue must have drained the previous segment's accumulators
@@ -268,20 +281,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         }
         if (!mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull)) { s_bail = 1; break; }
         tc_fence_after();
+        DBK_MARK(lane == 0 && j == 0, 4);
+        DBK_MARK(lane == 0 && j == 32, 9);
         if (lane == 0) {
           const uint32_t st = smem_u32(smem + (size_t)s * a.stage_bytes);
+          const uint64_t da0 = sw128_desc(st);
+          const uint64_t dw0 = sw128_desc(st + a_bytes);
 #pragma unroll
-          for (int acc = 0; acc < NACC; ++acc) {
+          for (int k = 0; k < kBK / 16; ++k) {
 #pragma unroll
-            for (int part = 0; part < NB; ++part) {
-#pragma unroll
-              for (int k = 0; k < kBK / 16; ++k) {
-                const uint64_t da = sw128_desc(st + acc * a_bytes + k * 32);
-                const uint64_t db = sw128_desc(st + NACC * a_bytes + part * b_bytes + k * 32);
-                const uint32_t accumulate = (first && part == 0 && k == 0) ? 0u : 1u;
-                umma(tmem + acc * N, da, db, idesc, accumulate);
-              }
-            }
+            for (int acc = 0; acc < NACC; ++acc)
+              umma(tmem + acc * kBN, da0 + (uint64_t)(k * 2),
+                   dw0 + (uint64_t)((acc * w_bytes + k * 32) >> 4), idesc,
+                   (first && k == 0) ? 0u : 1u);
           }
           umma_commit(&empty[s]);           // stage free once these MMAs have read it
         }
@@ -289,6 +301,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         first = false;
         const bool seg_end = (kb == a.kblocks - 1) || (j == u1 - u0 - 1);
         if (seg_end) {
+          DBK_MARK(lane == 0, seg == 0 ? 5 : 10);
           if (lane == 0) umma_commit(acc_full);
           __syncwarp();
           ++seg;
@@ -300,46 +313,59 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     // ------------------------------------------------------------ epilogue (warps 2..5)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
-    const int row_local = quarter * 32 + lane;    // m-tile row of this thread
+    const int r = quarter * 32 + lane;            // A row = activation row of this thread
     const int etid = tid - 64;                    // 0..127
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
     T* y = static_cast<T*>(a.y);
     const T* res = static_cast<const T*>(a.residual);
+    const bool owner_row = r < a.batch;           // holds (the hi part of) batch row r
+    // D columns gq*16 .. +15 of accumulator acc, hi + lo summed on the owner rows.
+    auto gather = [&](int acc, int gq, float (&v)[16]) {
+      tmem_ld16(trow + acc * kBN + gq * 16, v);
+      if constexpr (SPLIT) {
+        if (r >= a.nb && r < a.nb + a.batch)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) xbuf[r - a.nb][i] = v[i];
+        named_bar_sync(1, 128);
+        if (owner_row)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] += xbuf[r][i];
+        named_bar_sync(1, 128);
+      }
+    };
     int seg = 0;
     for (int j0 = 0; active && j0 < u1 - u0 && !s_bail;) {
-      const int u = u0 + j0, mt = u / a.kblocks, kb0 = u - mt * a.kblocks;
+      const int u = u0 + j0, nt = u / a.kblocks, kb0 = u - nt * a.kblocks;
       const int len = min(a.kblocks - kb0, u1 - u);       // units of this segment
       if (!mbar_wait(acc_full, seg & 1, kDevTimeoutMma)) { s_bail = 1; break; }
       tc_fence_after();
-      const int ngrp = N / 16;
+      DBK_MARK(etid == 0, seg == 0 ? 6 : 11);
       const bool whole = (kb0 == 0) && (len == a.kblocks);
-      const int row = mt * kBM + row_local;
-      const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-      // Epilogue of 16 batch columns (gq) for this thread's output row.
-      auto finish = [&](int gq, const float (&g0)[16], const float (&g1)[16]) {
-        if (row >= a.d_out) return;
+      const int col0 = nt * kBN;
+      // Epilogue of batch row b, weight rows col0 + gq*16 .. +15.
+      auto finish_row = [&](int b, int gq, const float (&g0)[16], const float (&g1)[16]) {
+        const float scb = a.inv_rms ? a.inv_rms[b] : 1.f;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int b = gq * 16 + i;
-          if (b >= a.batch) break;
+          const int c = col0 + gq * 16 + i;
+          if (c >= a.d_out) break;
           float val;
-          if constexpr (MODE == TC_SWIGLU) {
-            const float sc = a.inv_rms ? a.inv_rms[b] : 1.f;
-            val = silu(g0[i] * sc) * (g1[i] * sc);
-          } else if constexpr (MODE == TC_NORM) {
-            val = g0[i] * a.inv_rms[b];
-          } else {
-            val = g0[i];
-          }
-          const size_t o = (size_t)b * a.d_out + row;
+          if constexpr (MODE == TC_SWIGLU) val = silu(g0[i] * scb) * (g1[i] * scb);
+          else if constexpr (MODE == TC_NORM) val = g0[i] * scb;
+          else val = g0[i];
+          const size_t o = (size_t)b * a.d_out + c;
           if (res != nullptr) val += Elem<T>::to_f(res[o]);
           y[o] = Elem<T>::from_f(val);
         }
       };
+      auto finish = [&](int gq, const float (&g0)[16], const float (&g1)[16]) {
+        if (owner_row) finish_row(r, gq, g0, g1);
+      };
       if (whole) {
-        for (int gq = 0; gq < ngrp; ++gq) {
+        for (int gq = 0; gq < kBN / 16; ++gq) {
           float g0[16], g1[16];
-          tmem_ld16(trow + gq * 16, g0);
-          if constexpr (NACC == 2) tmem_ld16(trow + N + gq * 16, g1);
+          gather(0, gq, g0);
+          if constexpr (NACC == 2) gather(1, gq, g1);
           finish(gq, g0, g1);
         }
         tc_fence_before();
@@ -349,18 +375,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         ++seg;
         continue;
       }
-      // Partial m-tile: publish this CTA's fp32 partial; the last contributor merges.
+      // Partial tile: publish this CTA's fp32 partial; the last contributor merges.
       const int slot = 2 * blockIdx.x + (u == u0 ? 0 : 1);
-      float* dst = a.part + ((size_t)slot * NACC * kBM + row_local) * N;
-      for (int gq = 0; gq < ngrp; ++gq) {
+      for (int gq = 0; gq < kBN / 16; ++gq) {
 #pragma unroll
         for (int acc = 0; acc < NACC; ++acc) {
           float g0[16];
-          tmem_ld16(trow + acc * N + gq * 16, g0);
+          gather(acc, gq, g0);
+          if (owner_row) {
+            float* dst = a.part + (((size_t)slot * NACC + acc) * a.batch + r) * kBN + gq * 16;
 #pragma unroll
-          for (int i = 0; i < 16; i += 4)
-            *reinterpret_cast<float4*>(dst + (size_t)acc * kBM * N + gq * 16 + i) =
-                make_float4(g0[i], g0[i + 1], g0[i + 2], g0[i + 3]);
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(dst + i) = make_float4(g0[i], g0[i + 1], g0[i + 2], g0[i + 3]);
+          }
         }
       }
       tc_fence_before();
@@ -368,80 +395,100 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       if (lane == 0) mbar_arrive(acc_empty);
       __threadfence();
       named_bar_sync(1, 128);
-      const int first_u = mt * a.kblocks, last_u = first_u + a.kblocks - 1;
+      const int first_u = nt * a.kblocks, last_u = first_u + a.kblocks - 1;
       const int c_first = owner(first_u, U, G), c_last = owner(last_u, U, G);
       if (etid == 0) {
-        const int prev = atomicAdd(&a.done[mt], 1);
-        s_last[0] = (prev == c_last - c_first);
+        const int prev = atomicAdd(&a.done[nt], 1);
+        s_last = (prev == c_last - c_first);
       }
       named_bar_sync(1, 128);
-      const bool last = s_last[0] != 0;
+      const bool last = s_last != 0;
       named_bar_sync(1, 128);                   // s_last is rewritten by the next segment
       if (last) {
         __threadfence();
-        for (int gq = 0; gq < ngrp; ++gq) {
+        // All 128 epilogue threads share the merge: item = (batch row, 16 columns).
+        for (int it = etid; it < a.batch * (kBN / 16); it += 128) {
+          const int b = it / (kBN / 16), gq = it - b * (kBN / 16);
           float g0[16], g1[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) g0[i] = g1[i] = 0.f;
+#pragma unroll 2
           for (int c = c_first; c <= c_last; ++c) {
             const int sl = 2 * c + (range_start(c, U, G) >= first_u ? 0 : 1);
-            const float* src = a.part + ((size_t)sl * NACC * kBM + row_local) * N + gq * 16;
 #pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-              const float4 p0 = __ldcg(reinterpret_cast<const float4*>(src + i));
-              g0[i] += p0.x; g0[i + 1] += p0.y; g0[i + 2] += p0.z; g0[i + 3] += p0.w;
-              if constexpr (NACC == 2) {
-                const float4 p1 = __ldcg(reinterpret_cast<const float4*>(src + (size_t)kBM * N + i));
-                g1[i] += p1.x; g1[i + 1] += p1.y; g1[i + 2] += p1.z; g1[i + 3] += p1.w;
+            for (int acc = 0; acc < NACC; ++acc) {
+              const float* src = a.part + (((size_t)sl * NACC + acc) * a.batch + b) * kBN + gq * 16;
+              float4 p4[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) p4[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
+              float* g = acc ? g1 : g0;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                g[4 * i] += p4[i].x; g[4 * i + 1] += p4[i].y;
+                g[4 * i + 2] += p4[i].z; g[4 * i + 3] += p4[i].w;
               }
             }
           }
-          finish(gq, g0, g1);
+          finish_row(b, gq, g0, g1);
         }
-        if (etid == 0) a.done[mt] = 0;        // ready for the next launch
+        if (etid == 0) a.done[nt] = 0;        // ready for the next launch
       }
       j0 += len;
       ++seg;
     }
   }
+  DBK_MARK(tid == 64, 7);
+  // Teardown: each warp arrives once, converged, on an mbarrier; warp 1 waits
+  // for all six and then frees TMEM. (A CTA-wide bar.sync after this
+  // warp-specialised, divergent code let warps pass before the epilogue had
+  // finished, and the TMEM release then stalled.)
+  __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  DBK_MARK(tid == 0, 14);
+  DBK_MARK(tid == 160, 15);
+  if (lane == 0) mbar_arrive(teardown);
   if (warp == 1) {
+    mbar_wait(teardown, 0, kDevTimeoutDrain);
     tc_fence_after();
+    DBK_MARK(lane == 0, 8);
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
                  ::"r"(tmem), "r"(a.tmem_cols) : "memory");
+    DBK_MARK(lane == 0, 12);
   }
 }
 
 // ---------------------------------------------------------------- host side
 struct TcPlan {
-  int n, mtiles, kblocks, grid, nstages, stage_bytes;
+  int nb, rows, ntiles, kblocks, grid, nstages, stage_bytes;
   uint32_t tmem_cols;
   size_t smem, ws_b, ws_rms, ws_part, ws_done, ws_total;
 };
+
+// One pass handles up to kMaxRows A rows: batch <= 128, or <= 64 with a hi/lo split.
+int pass_batch(bool split) { return split ? kMaxRows / 2 : kMaxRows; }
 
 TcPlan make_plan(int mode, bool split, int batch, int d_in, int d_out, int num_sms,
                  int smem_optin) {
   TcPlan p{};
   const int nacc = (mode == TC_SWIGLU) ? 2 : 1;
-  p.n = ((batch + 15) / 16) * 16;
-  p.mtiles = (d_out + kBM - 1) / kBM;
+  p.nb = ((batch + 7) / 8) * 8;
+  p.rows = split ? 2 * p.nb : p.nb;
+  p.ntiles = (d_out + kBN - 1) / kBN;
   p.kblocks = (d_in + kBK - 1) / kBK;
-  const int64_t U = (int64_t)p.mtiles * p.kblocks;
+  const int64_t U = (int64_t)p.ntiles * p.kblocks;
   p.grid = (int)(U < num_sms ? U : num_sms);
-  p.stage_bytes = nacc * kBM * kBK * 2 + (split ? 2 : 1) * p.n * kBK * 2;
-  const size_t fixed = 1024 + 256;
-  p.nstages = 8;
-  while (p.nstages > 2 && fixed + (size_t)p.nstages * p.stage_bytes > (size_t)smem_optin - 1024)
+  p.stage_bytes = p.rows * 128 + nacc * kBN * 128;
+  static const int env_st = [] { const char* v = std::getenv("DBK_TC_STAGES"); return v ? std::atoi(v) : 12; }();
+  const size_t fixed = 1024 + 512;
+  p.nstages = env_st < 2 ? 2 : (env_st > 12 ? 12 : env_st);
+  while (p.nstages > 2 && fixed + (size_t)p.nstages * p.stage_bytes > (size_t)smem_optin - 4096)
     --p.nstages;
   p.smem = fixed + (size_t)p.nstages * p.stage_bytes;
-  uint32_t cols = 32;
-  while (cols < (uint32_t)(nacc * p.n)) cols <<= 1;
-  p.tmem_cols = cols;
-  p.ws_b = split ? (size_t)2 * p.n * d_in * 2 : 0;
-  p.ws_rms = (size_t)p.n * sizeof(float);
-  p.ws_part = (size_t)2 * num_sms * nacc * kBM * p.n * sizeof(float);
-  p.ws_done = (size_t)p.mtiles * sizeof(int);
+  p.tmem_cols = (uint32_t)(nacc * kBN);
+  p.ws_b = split ? (size_t)2 * p.nb * d_in * 2 : 0;
+  p.ws_rms = (size_t)p.nb * sizeof(float);
+  p.ws_part = (size_t)2 * num_sms * nacc * batch * kBN * sizeof(float);
+  p.ws_done = (size_t)p.ntiles * sizeof(int);
   p.ws_total = ((p.ws_b + 255) & ~(size_t)255) + ((p.ws_rms + 255) & ~(size_t)255) +
                ((p.ws_part + 255) & ~(size_t)255) + ((p.ws_done + 255) & ~(size_t)255);
   return p;
@@ -456,14 +503,11 @@ int launch_tc(TcArgs& a, const TcPlan& p, cudaStream_t st) {
                     &a);
 }
 
+// One pass: batch <= pass_batch(split).
 template <typename T>
-int tc_run(int mode, const void* x, const void* gamma, const void* W0, const void* W1,
-           const void* residual, void* y, int batch, int d_in, int d_out, float eps, int dtype,
-           void* ws, size_t ws_bytes, void* stream) {
-  if (batch > kMaxN) return DBK_ESHAPE;
-  DeviceInfo dev;
-  int rc = current_device_info(&dev);
-  if (rc) return rc;
+int tc_pass(int mode, const void* x, const void* gamma, const void* W0, const void* W1,
+            const void* residual, void* y, int batch, int d_in, int d_out, float eps, int dtype,
+            void* ws, size_t ws_bytes, cudaStream_t st, const DeviceInfo& dev) {
   const bool split = (gamma != nullptr);     // x alone is exact in 16 bits
   const TcPlan p = make_plan(mode, split, batch, d_in, d_out, dev.num_sms, dev.max_smem_optin);
   if (p.smem > (size_t)dev.max_smem_optin) return DBK_ESHAPE;
@@ -472,27 +516,24 @@ int tc_run(int mode, const void* x, const void* gamma, const void* W0, const voi
   uint8_t* w = static_cast<uint8_t*>(ws);
   auto take = [&](size_t n) { uint8_t* r = w; w += (n + 255) & ~(size_t)255; return r; };
   T* b_hi = reinterpret_cast<T*>(take(p.ws_b));
-  T* b_lo = b_hi + (size_t)p.n * d_in;
+  T* b_lo = b_hi + (size_t)p.nb * d_in;
   float* rms = reinterpret_cast<float*>(take(p.ws_rms));
   float* part = reinterpret_cast<float*>(take(p.ws_part));
   int* done = reinterpret_cast<int*>(take(p.ws_done));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   TcArgs a{};
   a.residual = residual; a.y = y; a.part = part; a.done = done;
   a.inv_rms = split ? rms : nullptr;
-  a.batch = batch; a.n = p.n; a.d_in = d_in; a.d_out = d_out;
-  a.mtiles = p.mtiles; a.kblocks = p.kblocks; a.nstages = p.nstages; a.stage_bytes = p.stage_bytes;
+  a.batch = batch; a.nb = p.nb; a.rows = p.rows; a.d_in = d_in; a.d_out = d_out;
+  a.ntiles = p.ntiles; a.kblocks = p.kblocks; a.nstages = p.nstages; a.stage_bytes = p.stage_bytes;
   a.tmem_cols = p.tmem_cols;
   const uint64_t rs = (uint64_t)d_in * 2;
-  if ((rc = encode_tmap_2d(&a.wmap0, W0, dtype, d_in, d_out, rs, kBK, kBM, true))) return rc;
-  if (mode == TC_SWIGLU && (rc = encode_tmap_2d(&a.wmap1, W1, dtype, d_in, d_out, rs, kBK, kBM, true)))
+  int rc;
+  if ((rc = encode_tmap_2d(&a.wmap0, W0, dtype, d_in, d_out, rs, kBK, kBN, true))) return rc;
+  if (mode == TC_SWIGLU && (rc = encode_tmap_2d(&a.wmap1, W1, dtype, d_in, d_out, rs, kBK, kBN, true)))
     return rc;
   if (split) {
-    if ((rc = encode_tmap_2d(&a.bmap, b_hi, dtype, d_in, p.n, rs, kBK, p.n, true))) return rc;
-    if ((rc = encode_tmap_2d(&a.bmap_lo, b_lo, dtype, d_in, p.n, rs, kBK, p.n, true))) return rc;
-    struct PrepArgs { const T* x; const T* g; T* hi; T* lo; float* rms; int batch, d_in; float eps; };
-    // One CTA per B row (rows >= batch are written as zeros).
+    if ((rc = encode_tmap_2d(&a.amap, b_hi, dtype, d_in, p.rows, rs, kBK, p.rows, true))) return rc;
     void* args[8];
     const T* xx = static_cast<const T*>(x);
     const T* gg = static_cast<const T*>(gamma);
@@ -501,7 +542,7 @@ int tc_run(int mode, const void* x, const void* gamma, const void* W0, const voi
     args[0] = &xx; args[1] = &gg; args[2] = &b_hi; args[3] = &b_lo; args[4] = &rms;
     args[5] = &bb; args[6] = &dd; args[7] = &ee;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(p.n);
+    cfg.gridDim = dim3(p.nb);                 // one CTA per hi row (rows >= batch: zeros)
     cfg.blockDim = dim3(256);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -512,7 +553,7 @@ int tc_run(int mode, const void* x, const void* gamma, const void* W0, const voi
     cudaError_t e = cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(tc_prep_kernel<T>), args);
     if (e != cudaSuccess) return (int)e;
   } else {
-    if ((rc = encode_tmap_2d(&a.bmap, x, dtype, d_in, batch, rs, kBK, p.n, true))) return rc;
+    if ((rc = encode_tmap_2d(&a.amap, x, dtype, d_in, batch, rs, kBK, p.rows, true))) return rc;
   }
   switch (mode) {
     case TC_PLAIN:
@@ -522,6 +563,29 @@ int tc_run(int mode, const void* x, const void* gamma, const void* W0, const voi
     default:
       return split ? launch_tc<T, TC_SWIGLU, true>(a, p, st) : launch_tc<T, TC_SWIGLU, false>(a, p, st);
   }
+}
+
+// Batches beyond one pass run as consecutive passes over row slices of x / y.
+template <typename T>
+int tc_run(int mode, const void* x, const void* gamma, const void* W0, const void* W1,
+           const void* residual, void* y, int batch, int d_in, int d_out, float eps, int dtype,
+           void* ws, size_t ws_bytes, void* stream) {
+  if (batch > 256) return DBK_ESHAPE;
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc) return rc;
+  const int pb = pass_batch(gamma != nullptr);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int b0 = 0; b0 < batch; b0 += pb) {
+    const int nb = batch - b0 < pb ? batch - b0 : pb;
+    const T* xs = static_cast<const T*>(x) + (size_t)b0 * d_in;
+    const T* rsd = residual ? static_cast<const T*>(residual) + (size_t)b0 * d_out : nullptr;
+    T* ys = static_cast<T*>(y) + (size_t)b0 * d_out;
+    rc = tc_pass<T>(mode, xs, gamma, W0, W1, rsd, ys, nb, d_in, d_out, eps, dtype, ws, ws_bytes, st,
+                    dev);
+    if (rc) return rc;
+  }
+  return DBK_OK;
 }
 
 int tc_dispatch(int mode, const void* x, const void* gamma, const void* W0, const void* W1,
@@ -562,13 +626,18 @@ int dbk_tc_gemv(const void* x, const void* W, const void* residual, void* y, int
 }
 
 size_t dbk_tc_workspace_bytes(int op, int64_t batch, int64_t d_in, int64_t d_out) {
-  if (batch < 1 || batch > kMaxN || d_in < 8 || d_out < 1) return 0;
+  if (batch < 1 || batch > 256 || d_in < 8 || d_out < 1) return 0;
   DeviceInfo dev;
   int nsm = 148, optin = 232448;
   if (current_device_info(&dev) == DBK_OK) { nsm = dev.num_sms; optin = dev.max_smem_optin; }
   const int mode = op == DBK_OP_GATEUP_SWIGLU ? TC_SWIGLU : op == DBK_OP_RMSNORM_GEMV ? TC_NORM : TC_PLAIN;
-  // Sized for the split (gamma) case, which needs the most.
-  return make_plan(mode, mode != TC_PLAIN, (int)batch, (int)d_in, (int)d_out, nsm, optin).ws_total;
+  // Sized for one pass of the split (gamma) case, which needs the most.
+  const bool split = mode != TC_PLAIN;
+  const int pb = (int)(batch < pass_batch(split) ? batch : pass_batch(split));
+  const size_t a = make_plan(mode, split, pb, (int)d_in, (int)d_out, nsm, optin).ws_total;
+  const size_t b = make_plan(mode, false, (int)(batch < pass_batch(false) ? batch : pass_batch(false)),
+                             (int)d_in, (int)d_out, nsm, optin).ws_total;
+  return a > b ? a : b;
 }
 
 extern "C" size_t dbk_workspace_bytes(int op, int64_t batch, int64_t d_in, int64_t d_out) {
