@@ -576,22 +576,44 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
     named_bar_sync(1, kConsumers);
     if (!s_last) continue;
     __threadfence();
-    for (int idx = tid; idx < G * kD; idx += kConsumers) {
-      const int g = idx / kD, d = idx - g * kD;
-      float M = -INFINITY;
-      for (int c = c_first; c <= c_last; ++c) {
+    {
+      // Merge the row's partials: (m, l) of every contributor loaded in parallel
+      // into shared memory (mrg is free again), weights computed once per head,
+      // then every thread sums its output elements with independent loads.
+      const int np = c_last - c_first + 1;
+      float* wm = mrg;                          // [np][G]: m, then the weight e^(m - M)
+      float* wl = mrg + np * G;                 // [np][G]: l
+      float* inv_l = wl + np * G;               // [G]
+      int* slot_of = reinterpret_cast<int*>(inv_l + G);   // [np]
+      for (int i = tid; i < np * G; i += kConsumers) {
+        const int c = c_first + i / G, g = i % G;
         const int sl = 2 * c + (range_start(c, Ttot, grid) >= rs ? 0 : 1);
-        M = fmaxf(M, __ldcg(&a.part_ml[(size_t)sl * G + g].x));
-      }
-      float L = 0.f, O = 0.f;
-      for (int c = c_first; c <= c_last; ++c) {
-        const int sl = 2 * c + (range_start(c, Ttot, grid) >= rs ? 0 : 1);
+        if (g == 0) slot_of[i / G] = sl;
         const float2 ml = __ldcg(&a.part_ml[(size_t)sl * G + g]);
-        const float f = exp2f(ml.x - M);
-        L = fmaf(f, ml.y, L);
-        O = fmaf(f, __ldcg(&a.part_o[((size_t)sl * G + g) * kD + d]), O);
+        wm[i] = ml.x;
+        wl[i] = ml.y;
       }
-      out[((size_t)w.b * a.hq + (size_t)w.hk * G + g) * kD + d] = Elem<T>::from_f(O / L);
+      named_bar_sync(1, kConsumers);
+      if (tid < G) {
+        float M = -INFINITY;
+        for (int c = 0; c < np; ++c) M = fmaxf(M, wm[c * G + tid]);
+        float L = 0.f;
+        for (int c = 0; c < np; ++c) {
+          const float f = exp2f(wm[c * G + tid] - M);
+          wm[c * G + tid] = f;
+          L = fmaf(f, wl[c * G + tid], L);
+        }
+        inv_l[tid] = 1.f / L;
+      }
+      named_bar_sync(1, kConsumers);
+      for (int idx = tid; idx < G * kD; idx += kConsumers) {
+        const int g = idx / kD, d = idx - g * kD;
+        float O = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < np; ++c)
+          O = fmaf(wm[c * G + g], __ldcg(&a.part_o[((size_t)slot_of[c] * G + g) * kD + d]), O);
+        out[((size_t)w.b * a.hq + (size_t)w.hk * G + g) * kD + d] = Elem<T>::from_f(O * inv_l[g]);
+      }
     }
     if (tid == 0) a.done[w.row()] = 0;   // ready for the next launch
     DBK_MARK(tid == 0, 7);
