@@ -460,6 +460,10 @@ class GQA(F4):
         K, V = self.KV[rep % self.nrep]
         self.ops.flashdecode(self.q, K, V, seq_lens=self.lens, page_table=self.table, out=self.o)
 
+    def exchange(self):
+        if self.world > 1:
+            self.t.distributed.all_gather_into_tensor(self.o_full, self.o)
+
     def e2e_setup(self):
         t = self.t
         self.q_host = self.q_cpu.pin_memory()
@@ -769,7 +773,10 @@ def main() -> int:
 
     if world > 1:
         torch.cuda.set_device(local)
-        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+        import datetime
+
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                             timeout=datetime.timedelta(seconds=120))
     else:
         torch.cuda.set_device(0)
     dev_index = torch.cuda.current_device()
@@ -788,9 +795,14 @@ def main() -> int:
     t_end = time.perf_counter()
     # Keep identical steps running until the sampler has seen >= 5 samples, so
     # that a short timed region still has a clock record around it.
+    # The graphs hold collectives, so every rank must replay the same number of
+    # times: the decision to pad once more is agreed (max over ranks) each round.
     pad_until = time.perf_counter() + 2.0
-    while sampler.ok and sampler.count_between(t_begin, time.perf_counter()) < 5 \
-            and time.perf_counter() < pad_until:
+    while True:
+        need = (sampler.ok and sampler.count_between(t_begin, time.perf_counter()) < 5
+                and time.perf_counter() < pad_until)
+        if dist_max(torch, float(need)) == 0.0:
+            break
         graphs.run(256)
         torch.cuda.synchronize()
     clocks = sampler.summary(t_begin, max(t_end, time.perf_counter()))

@@ -3,6 +3,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "dbk_internal.h"
@@ -47,6 +48,25 @@ int current_device_info(DeviceInfo* out) {
   }
   if (g_info[dev].cc_major != 10) return DBK_EDEVICE;
   *out = g_info[dev];
+  return DBK_OK;
+}
+
+namespace {
+std::mutex g_attr_mu;
+std::vector<std::pair<const void*, int>> g_attr_done;   // (kernel, device) pairs already raised
+}  // namespace
+
+int allow_dynamic_smem(const void* kern, const DeviceInfo& dev, size_t smem) {
+  if (smem > (size_t)dev.max_smem_optin) return DBK_ESHAPE;
+  if (smem <= 48 * 1024) return DBK_OK;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  for (const auto& kd : g_attr_done)
+    if (kd.first == kern && kd.second == dev.device) return DBK_OK;
+  // Raise the limit to the device maximum once; launches then pass their own size.
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       dev.max_smem_optin);
+  if (e != cudaSuccess) return (int)e;
+  g_attr_done.emplace_back(kern, dev.device);
   return DBK_OK;
 }
 

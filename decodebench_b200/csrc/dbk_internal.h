@@ -22,6 +22,9 @@ struct DeviceInfo {
 
 // Cached per-device properties of the current device; DBK_EDEVICE if not sm_100.
 int current_device_info(DeviceInfo* out);
+// Lets `kern` launch with up to the device's opt-in shared memory (once per kernel and
+// device; later calls only check `smem` against the limit).
+int allow_dynamic_smem(const void* kern, const DeviceInfo& dev, size_t smem);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

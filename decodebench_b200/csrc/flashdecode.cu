@@ -350,11 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
         if (!mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull)) return;
         DBK_MARK(lane == 0 && warp == 0 && j == 0, 3);
         DBK_MARK(lane == 0 && warp == 0 && j == 16, 4);
-#ifdef DBK_FD_SKIP
-        const int t0 = kTile;                   // dev experiment: stream only
-#else
         const int t0 = wi * 16;                 // this warp's 16 tokens
-#endif
         if (t0 < n) {
           if (n < kTile && t0 + 16 > n) {
             // ragged tail: zero this warp's V rows >= n (their probabilities are 0,
@@ -644,8 +640,7 @@ int launch_g(FdArgs a, cudaStream_t st, const DeviceInfo& dev, int grid, bool mm
   const size_t smem = (size_t)nst * (kStage + 16) + fixed;
   if (smem > (size_t)dev.max_smem_optin) return DBK_ESHAPE;
   auto kern = mma ? flashdecode_kernel<T, G, true> : flashdecode_kernel<T, G, false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return (int)e;
+  if (int rc = allow_dynamic_smem(reinterpret_cast<const void*>(kern), dev, smem)) return rc;
   return launch_pdl(reinterpret_cast<const void*>(kern), dim3(grid), dim3(kThreads), smem, st, &a);
 }
 

@@ -495,10 +495,9 @@ TcPlan make_plan(int mode, bool split, int batch, int d_in, int d_out, int num_s
 }
 
 template <typename T, int MODE, bool SPLIT>
-int launch_tc(TcArgs& a, const TcPlan& p, cudaStream_t st) {
+int launch_tc(TcArgs& a, const TcPlan& p, cudaStream_t st, const DeviceInfo& dev) {
   auto kern = tc_gemm_kernel<T, MODE, SPLIT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-  if (e != cudaSuccess) return (int)e;
+  if (int rc = allow_dynamic_smem(reinterpret_cast<const void*>(kern), dev, p.smem)) return rc;
   return launch_pdl(reinterpret_cast<const void*>(kern), dim3(p.grid), dim3(kTcThreads), p.smem, st,
                     &a);
 }
@@ -557,11 +556,11 @@ int tc_pass(int mode, const void* x, const void* gamma, const void* W0, const vo
   }
   switch (mode) {
     case TC_PLAIN:
-      return split ? launch_tc<T, TC_PLAIN, true>(a, p, st) : launch_tc<T, TC_PLAIN, false>(a, p, st);
+      return split ? launch_tc<T, TC_PLAIN, true>(a, p, st, dev) : launch_tc<T, TC_PLAIN, false>(a, p, st, dev);
     case TC_NORM:
-      return launch_tc<T, TC_NORM, true>(a, p, st);
+      return launch_tc<T, TC_NORM, true>(a, p, st, dev);
     default:
-      return split ? launch_tc<T, TC_SWIGLU, true>(a, p, st) : launch_tc<T, TC_SWIGLU, false>(a, p, st);
+      return split ? launch_tc<T, TC_SWIGLU, true>(a, p, st, dev) : launch_tc<T, TC_SWIGLU, false>(a, p, st, dev);
   }
 }
 

@@ -495,8 +495,7 @@ int launch_mma(GemvArgs a, cudaStream_t st, const DeviceInfo& dev, size_t smem) 
   const void* kern = (a.gamma != nullptr)   // x alone is exact in 16 bits: no low part
                          ? reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, true>)
                          : reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, false>);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return (int)e;
+  if (int rc = allow_dynamic_smem(reinterpret_cast<const void*>(kern), dev, smem)) return rc;
   return launch_pdl(kern, dim3(a.d_out < dev.num_sms ? a.d_out : dev.num_sms), dim3(kThreads),
                     smem, st, &a);
 }
@@ -521,8 +520,7 @@ int launch_nb(GemvArgs a, cudaStream_t st, const DeviceInfo& dev) {
   if (smem > (size_t)dev.max_smem_optin) return DBK_ESHAPE;
 
   auto kern = gemv_stream_kernel<T, NB, MODE, KCG>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return (int)e;
+  if (int rc = allow_dynamic_smem(reinterpret_cast<const void*>(kern), dev, smem)) return rc;
   return launch_pdl(reinterpret_cast<const void*>(kern), dim3(grid), dim3(kThreads), smem, st, &a);
 }
 

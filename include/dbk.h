@@ -73,7 +73,8 @@ size_t dbk_flashdecode_workspace_bytes(int batch, int n_q_heads, int n_kv_heads,
  * Replaces fused f1_kernel (validation/src/kernels/fused/f1.cu:18-84, launched at
  * bench_variant.cu:379-387) and the Python stages rmsnorm + gemv
  * (src/decodebench/demos/llama_decode.py:36-43).
- * batch 1..8 on CUDA cores; batch 9..256 on tcgen05 tensor cores (needs workspace). */
+ * batch 1..8: streaming kernel (mma.sync; CUDA cores when d_in % 16 != 0), no workspace;
+ * batch 9..256: tcgen05 tensor cores (needs workspace). */
 int dbk_rmsnorm_gemv(const void* x, const void* gamma, const void* W, void* y,
                      int batch, int d_in, int d_out, float eps, int dtype,
                      void* workspace, size_t workspace_bytes, void* stream);
