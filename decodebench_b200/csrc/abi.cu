@@ -53,7 +53,12 @@ int current_device_info(DeviceInfo* out) {
 
 namespace {
 std::mutex g_attr_mu;
-std::vector<std::pair<const void*, int>> g_attr_done;   // (kernel, device) pairs already raised
+struct AttrDone {
+  const void* kern;
+  int device;
+  int most;      // dynamic shared memory limit that was set
+};
+std::vector<AttrDone> g_attr_done;
 }  // namespace
 
 int allow_dynamic_smem(const void* kern, const DeviceInfo& dev, size_t smem) {
@@ -61,12 +66,18 @@ int allow_dynamic_smem(const void* kern, const DeviceInfo& dev, size_t smem) {
   if (smem <= 48 * 1024) return DBK_OK;
   std::lock_guard<std::mutex> lk(g_attr_mu);
   for (const auto& kd : g_attr_done)
-    if (kd.first == kern && kd.second == dev.device) return DBK_OK;
-  // Raise the limit to the device maximum once; launches then pass their own size.
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       dev.max_smem_optin);
+    if (kd.kern == kern && kd.device == dev.device)
+      return (long long)smem > kd.most ? DBK_ESHAPE : DBK_OK;
+  // Raise the limit to the most the kernel can have (the opt-in maximum less its
+  // static shared memory) once; launches then pass their own size.
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, kern);
   if (e != cudaSuccess) return (int)e;
-  g_attr_done.emplace_back(kern, dev.device);
+  const int most = dev.max_smem_optin - (int)fa.sharedSizeBytes;
+  if ((long long)smem > most) return DBK_ESHAPE;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+  if (e != cudaSuccess) return (int)e;
+  g_attr_done.push_back(AttrDone{kern, dev.device, most});
   return DBK_OK;
 }
 

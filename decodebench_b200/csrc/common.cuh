@@ -24,6 +24,7 @@ enum DeviceError : int {
   kDevTimeoutEmpty = 2,     // producer waited too long for a stage to drain
   kDevTimeoutMma = 3,       // waited too long for a tensor-core commit
   kDevTimeoutDrain = 4,     // waited too long for in-flight copies at exit
+  kDevTimeoutPeer = 5,      // waited too long for another GPU's all-gather signal
 };
 
 extern __device__ int dbk_device_error;
