@@ -139,6 +139,36 @@ class Workload:
     def e2e_setup(self) -> tuple[int, int]: ...
     def e2e_step(self) -> None: ...
 
+    with_exchange = True      # False while capturing the kernel-only (roofline) graphs
+    comm = None               # decodebench_b200.comm.PeerComm when the peer exchange is on
+    exchanges_per_step = 1    # shard-boundary all-gathers per step at N > 1
+
+    def xname(self) -> str:
+        return ("peer-store all-gather over NVLink (dbk_allgather)" if self.comm is not None
+                else "NCCL all-gather")
+
+    def gather_blocks(self, local, out=None):
+        """[*shape] per rank -> [world, *shape] in rank order."""
+        if self.comm is not None:
+            return self.comm.all_gather_blocks(local, out)
+        if out is None:
+            out = self.t.empty(self.world, *local.shape, dtype=local.dtype, device=local.device)
+        self.t.distributed.all_gather_into_tensor(out, local)
+        return out
+
+    def gather_rows(self, local, out=None):
+        """[rows, n] per rank -> [rows, world * n], rank p in columns [p n, (p + 1) n)."""
+        if self.comm is not None:
+            return self.comm.all_gather_rows(local, out)
+        rows, n = local.shape
+        full = self.t.empty(self.world, rows, n, dtype=local.dtype, device=local.device)
+        self.t.distributed.all_gather_into_tensor(full, local.contiguous())
+        res = full.permute(1, 0, 2).reshape(rows, self.world * n)
+        if out is None:
+            return res
+        out.copy_(res)
+        return out
+
 
 class F2(Workload):
     """x [1,4096] fp16, Wg/Wu [11008,4096] fp16 ~N(0,1)/64."""
@@ -174,7 +204,7 @@ class F2(Workload):
                             f"Wg/Wu [{self.d_ff},{self.d_in}] fp16 (BASELINE config 2)",
                 "global_batch": self.batch, "d_in": self.d_in, "d_ff": self.d_ff,
                 "parallelism": ("single GPU" if self.world == 1 else
-                                f"tp{self.world}: d_ff column-sharded, NCCL all-gather of h"),
+                                f"tp{self.world}: d_ff column-sharded, {self.xname()} of h"),
                 "weight_replicas": self.nrep,
                 "l2": f"weights rotated over {self.nrep} replicas "
                       f"({self.nrep * 2 * self.rows * self.d_in * 2 / 1e6:.0f} MB per GPU > 126 MB L2)"}
@@ -191,7 +221,7 @@ class F2(Workload):
 
     def exchange(self):
         if self.world > 1:
-            self.t.distributed.all_gather_into_tensor(self.h_full, self.h_local)
+            self.gather_blocks(self.h_local, self.h_full)
 
     def e2e_setup(self):
         t = self.t
@@ -207,9 +237,7 @@ class F2(Workload):
         self.x_dev.copy_(self.x_host, non_blocking=True)
         h = self.ops.gateup_swiglu(self.x_dev, Wg, Wu)
         if self.world > 1:
-            full = self.t.empty(self.world, *h.shape, dtype=h.dtype, device=h.device)
-            self.t.distributed.all_gather_into_tensor(full, h)
-            h = full
+            h = self.gather_blocks(h)
         self.out_host.copy_(h.reshape(-1), non_blocking=True)
 
     # reference CPU implementation (oracle/_ref: the reference's cpu_reference.cpp)
@@ -282,9 +310,7 @@ class F1(F2):
         self.x_dev.copy_(self.x_host, non_blocking=True)
         h = self.ops.rmsnorm_gemv(self.x_dev, self.gamma, W, eps=1e-6)
         if self.world > 1:
-            full = self.t.empty(self.world, *h.shape, dtype=h.dtype, device=h.device)
-            self.t.distributed.all_gather_into_tensor(full, h)
-            h = full
+            h = self.gather_blocks(h)
         self.out_host.copy_(h.reshape(-1), non_blocking=True)
 
     def cpu_setup(self, frac_rows: float = 1.0):
@@ -338,7 +364,7 @@ class F4(Workload):
                             f"K/V [{self.batch},{self.H},{self.L},128] fp16 (BASELINE config 3)",
                 "global_batch": self.batch, "heads": self.H, "kv_len": self.L,
                 "parallelism": ("single GPU" if self.world == 1 else
-                                f"heads sharded {self.h}/rank, NCCL all-gather of out"),
+                                f"heads sharded {self.h}/rank, {self.xname()} of out"),
                 "kv_replicas": self.nrep,
                 "l2": f"K/V rotated over {self.nrep} replicas"}
 
@@ -354,7 +380,7 @@ class F4(Workload):
 
     def exchange(self):
         if self.world > 1:
-            self.t.distributed.all_gather_into_tensor(self.o_full, self.o)
+            self.gather_blocks(self.o, self.o_full)
 
     def e2e_setup(self):
         t = self.t
@@ -370,9 +396,7 @@ class F4(Workload):
         self.q_dev.copy_(self.q_host, non_blocking=True)
         o = self.ops.flashdecode(self.q_dev, K, V)
         if self.world > 1:
-            full = self.t.empty(self.world, *o.shape, dtype=o.dtype, device=o.device)
-            self.t.distributed.all_gather_into_tensor(full, o)
-            o = full
+            o = self.gather_blocks(o)
         self.out_host.copy_(o.reshape(-1), non_blocking=True)
 
     def cpu_setup(self, frac_rows: float = 1.0):
@@ -435,7 +459,7 @@ class GQA(F4):
         self.q_cpu = torch.randn(batch, self.hq, 128, generator=xg).bfloat16()
         self.q = self.q_cpu.to(dev)
         self.o = torch.empty_like(self.q)
-        self.o_full = torch.empty(world, *self.o.shape, dtype=self.o.dtype, device=dev)
+        self.o_full = torch.empty(batch, hq, 128, dtype=self.o.dtype, device=dev)
         self.L = int(self.lens_np.max())
         self.H = hq
 
@@ -444,7 +468,7 @@ class GQA(F4):
                             "bf16, 64-token pages, lengths ~U[1024,32768] (BASELINE config 5)",
                 "global_batch": self.batch, "seq_lens": [int(x) for x in self.lens_np],
                 "parallelism": ("single GPU" if self.world == 1 else
-                                f"kv heads sharded {self.hkv}/rank, NCCL all-gather of out"),
+                                f"kv heads sharded {self.hkv}/rank, {self.xname()} of out"),
                 "kv_replicas": self.nrep, "l2": f"paged K/V {self.nrep} replica(s), "
                 f"{sum(t.nbytes for kv in self.KV for t in kv) / 1e6:.0f} MB > 126 MB L2"}
 
@@ -461,8 +485,9 @@ class GQA(F4):
         self.ops.flashdecode(self.q, K, V, seq_lens=self.lens, page_table=self.table, out=self.o)
 
     def exchange(self):
+        # [batch, Hq / N, D] per rank -> [batch, Hq, D], heads in rank order
         if self.world > 1:
-            self.t.distributed.all_gather_into_tensor(self.o_full, self.o)
+            self.gather_rows(self.o.view(self.batch, -1), self.o_full.view(self.batch, -1))
 
     def e2e_setup(self):
         t = self.t
@@ -478,9 +503,7 @@ class GQA(F4):
         self.q_dev.copy_(self.q_host, non_blocking=True)
         o = self.ops.flashdecode(self.q_dev, K, V, seq_lens=self.lens, page_table=self.table)
         if self.world > 1:
-            full = self.t.empty(self.world, *o.shape, dtype=o.dtype, device=o.device)
-            self.t.distributed.all_gather_into_tensor(full, o)
-            o = full
+            o = self.gather_rows(o.view(self.batch, -1))
         self.out_host.copy_(o.reshape(-1), non_blocking=True)
 
     def cpu_setup(self, frac_rows: float = 1.0):
@@ -506,7 +529,8 @@ class MLP(Workload):
     and down are column-sharded; h is all-gathered between them and y at the end."""
 
     name = "mlp"
-    kernels_per_step = 3   # prep, gate/up+SwiGLU, down (NCCL kernels at N > 1 not counted)
+    exchanges_per_step = 2
+    kernels_per_step = 3   # prep, gate/up+SwiGLU, down (exchanges counted separately)
 
     def __init__(self, rank, world, torch, batch=16, d=8192, d_ff=28672):
         from decodebench_b200 import costs, ops
@@ -525,18 +549,17 @@ class MLP(Workload):
         self.x = self.x_cpu.to(dev)
         self.gamma = torch.ones(d, dtype=torch.bfloat16, device=dev)
         self.h = torch.empty(batch, self.ff, dtype=torch.bfloat16, device=dev)
-        self.h_all = torch.empty(world, batch, self.ff, dtype=torch.bfloat16, device=dev)
         self.h_full = torch.empty(batch, d_ff, dtype=torch.bfloat16, device=dev)
         self.y = torch.empty(batch, self.dd, dtype=torch.bfloat16, device=dev)
-        self.y_all = torch.empty(world, batch, self.dd, dtype=torch.bfloat16, device=dev)
+        self.y_full = torch.empty(batch, d, dtype=torch.bfloat16, device=dev)
 
     def describe(self):
         return {"workload": "Llama-70B-shaped decode MLP, batch 16, d 8192, d_ff 28672, bf16: "
                             "RMSNorm -> gate/up -> SwiGLU -> down (BASELINE config 4)",
                 "global_batch": self.batch, "d_model": self.d, "d_ff": self.d_ff,
                 "parallelism": ("single GPU" if self.world == 1 else
-                                f"tp{self.world}: gate/up and down column-sharded, NCCL "
-                                "all-gather of h and of y"),
+                                f"tp{self.world}: gate/up and down column-sharded, "
+                                f"{self.xname()} of h and of y"),
                 "l2": "weights 1.41 GB / N per GPU, read once per step (> 126 MB L2)"}
 
     def step_bytes_total(self):
@@ -548,10 +571,9 @@ class MLP(Workload):
     def _gather_h(self):
         if self.world == 1:
             return self.h
-        self.t.distributed.all_gather_into_tensor(self.h_all, self.h)
-        # [world, batch, ff] -> [batch, world * ff]
-        self.h_full.copy_(self.h_all.permute(1, 0, 2).reshape(self.batch, self.d_ff))
-        return self.h_full
+        if not self.with_exchange:     # kernel-only timing: the down GEMV reads h_full as is
+            return self.h_full
+        return self.gather_rows(self.h, self.h_full)
 
     def run_kernel(self, rep):
         self.ops.gateup_swiglu(self.x, self.Wg, self.Wu, gamma=self.gamma, eps=1e-5, out=self.h)
@@ -559,7 +581,7 @@ class MLP(Workload):
 
     def exchange(self):
         if self.world > 1:
-            self.t.distributed.all_gather_into_tensor(self.y_all, self.y)
+            self.gather_rows(self.y, self.y_full)
 
     def e2e_setup(self):
         t = self.t
@@ -572,14 +594,10 @@ class MLP(Workload):
         self.x_dev.copy_(self.x_host, non_blocking=True)
         h = self.ops.gateup_swiglu(self.x_dev, self.Wg, self.Wu, gamma=self.gamma, eps=1e-5)
         if self.world > 1:
-            full = self.t.empty(self.world, *h.shape, dtype=h.dtype, device=h.device)
-            self.t.distributed.all_gather_into_tensor(full, h)
-            h = full.permute(1, 0, 2).reshape(self.batch, self.d_ff)
+            h = self.gather_rows(h)
         y = self.ops.gemv(h, self.Wd)
         if self.world > 1:
-            full = self.t.empty(self.world, *y.shape, dtype=y.dtype, device=y.device)
-            self.t.distributed.all_gather_into_tensor(full, y)
-            y = full
+            y = self.gather_rows(y)
         self.out_host.copy_(y.reshape(-1), non_blocking=True)
 
     def cpu_setup(self, frac_rows: float = 1.0):
@@ -642,6 +660,7 @@ class StepGraphs:
         self.torch = torch
 
         def one(r):
+            wl.with_exchange = with_exchange
             wl.run_kernel(r)
             if with_exchange:
                 wl.exchange()
@@ -783,6 +802,10 @@ def main() -> int:
 
     sys.path.insert(0, str(ROOT))
     wl = WORKLOADS[args.workload](rank, world, torch)
+    if world > 1 and os.environ.get("DBK_EXCHANGE", "peer") != "nccl":
+        from decodebench_b200.comm import PeerComm
+
+        wl.comm = PeerComm(8 << 20)       # largest block here: MLP h, 16 x 14336 bf16 at N=2
 
     # --- device-timed value: graphs of kernel + exchange, rotated over replicas
     graphs = StepGraphs(torch, wl, with_exchange=True)
@@ -849,11 +872,18 @@ def main() -> int:
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "fp16", "data": "synthetic, seeded (torch.Generator)",
                 "config": wl.describe(), "roofline": roofline, "cpu_baseline": cb, "e2e": e2e,
-                "clocks": clocks, "gpu_launches": args.steps * wl.kernels_per_step}
+                "clocks": clocks, "gpu_launches": args.steps * (wl.kernels_per_step + (
+                    wl.exchanges_per_step if world > 1 and wl.comm is not None else 0))}
         print(json.dumps(line))
     if world > 1:
+        # Every collective has completed (the e2e timing ended with a barrier and a
+        # max-reduce). The step graphs still hold NCCL work, and tearing the
+        # communicator down under them can block, so the ranks leave directly.
         torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+        torch.cuda.synchronize()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
     return 0
 
 

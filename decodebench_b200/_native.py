@@ -34,7 +34,15 @@ SIGNATURES = {
                              _P, _SZ, _P]),
     "dbk_flashdecode_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I,
                                      _P]),
+    "dbk_comm_buffer_bytes": (_SZ, [_SZ, _I]),
+    "dbk_comm_alloc": (_I, [_SZ, _I, ctypes.POINTER(_P), _P]),
+    "dbk_comm_open": (_I, [_I, _I, _P, _P, ctypes.POINTER(_P)]),
+    "dbk_comm_close": (_I, [_P]),
+    "dbk_comm_free": (_I, [_P]),
+    "dbk_allgather": (_I, [_P, _P, _P, _I, _SZ, _SZ, _SZ, _SZ, _P]),
 }
+
+DBK_COMM_RECORD_BYTES = 128
 
 _lib = None
 

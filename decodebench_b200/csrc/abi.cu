@@ -13,6 +13,12 @@ namespace dbk {
 __device__ int dbk_device_error = 0;
 #ifdef DBK_TRACE
 __device__ unsigned long long dbk_trace[2048 * 16];
+}  // namespace dbk
+// Development builds only: copies the phase timestamps to the host.
+extern "C" int dbk_trace_read(void* host, size_t bytes) {
+  return (int)cudaMemcpyFromSymbol(host, dbk::dbk_trace, bytes);
+}
+namespace dbk {
 #endif
 
 namespace {

@@ -133,6 +133,47 @@ int dbk_flashdecode_noalloc(const void* q, const void* k_cache, const void* v_ca
                             int page_size, int max_pages_per_seq, float scale, int dtype,
                             void* stream);
 
+/* ------------------------------------------------------------------------
+ * Shard-boundary all-gather over NVLink peer memory (multi-GPU, one process
+ * per GPU). No counterpart in the reference, which is single-GPU: it replaces
+ * the ncclAllGather that ends each sharded op (weight rows or kv heads split
+ * over the GPUs of one node). Setup, once per process group:
+ *   1. every rank: dbk_comm_alloc(capacity, world, &buf, record)  (cudaMalloc +
+ *      CUDA IPC handle; set-up time only, like a communicator's creation);
+ *   2. exchange the DBK_COMM_RECORD_BYTES records (rank order) out of band;
+ *   3. every rank: dbk_comm_open(rank, world, buf, records, &comm).
+ * Then dbk_allgather(comm, ...) on every rank, in the same order with the same
+ * sizes; teardown: dbk_comm_close on every rank, then dbk_comm_free.
+ * Ranks must be on different GPUs (dbk_comm_open returns DBK_EDEVICE
+ * otherwise). Waits on peers are bounded; a wait that gives up records a
+ * device error (dbk_take_device_error) and the kernel returns. */
+#define DBK_COMM_RECORD_BYTES 128
+typedef struct dbk_comm dbk_comm;
+
+/* Bytes of the comm buffer for `capacity_per_rank` bytes per block and `world` ranks. */
+size_t dbk_comm_buffer_bytes(size_t capacity_per_rank, int world);
+
+/* Allocates and zero-fills this rank's comm buffer on the current device and
+ * writes its DBK_COMM_RECORD_BYTES-byte record (IPC handle, GPU uuid, sizes). */
+int dbk_comm_alloc(size_t capacity_per_rank, int world, void** buf_out, void* record_out);
+
+/* Maps every peer's buffer; `records` holds world records in rank order. */
+int dbk_comm_open(int rank, int world, void* local_buf, const void* records, dbk_comm** out);
+int dbk_comm_close(dbk_comm* comm);
+int dbk_comm_free(void* buf);
+
+/* All-gather of equal blocks: this rank's block is `rows` rows of `row_bytes`
+ * bytes, `src_ld` bytes apart at `src`; rank p's row i is written to
+ *   out + p * out_block + i * out_ld
+ * on every rank (so [world][block] when out_block = block bytes, or blocks side
+ * by side in each row of [rows][world * row] when out_ld = world * row_bytes and
+ * out_block = row_bytes). row_bytes, the strides and both pointers must be
+ * 16-byte multiples; rows * row_bytes <= capacity_per_rank. Stream-ordered,
+ * no host synchronisation. Replaces ncclAllGather(src, out, ...) at the shard
+ * boundary. */
+int dbk_allgather(dbk_comm* comm, const void* src, void* out, int rows, size_t row_bytes,
+                  size_t src_ld, size_t out_ld, size_t out_block, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -54,3 +54,12 @@ def test_ops_refuse_cpu_tensors():
 
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         ops.gemv(torch.zeros(1, 16, dtype=torch.float16), torch.zeros(4, 16, dtype=torch.float16))
+
+
+def test_comm_host_checks():
+    lib = N.load()
+    assert lib.dbk_comm_buffer_bytes(1000, 2) == 10496 + 2 * 2 * 1024
+    assert lib.dbk_comm_buffer_bytes(1000, 9) == 0               # at most 8 ranks
+    assert lib.dbk_allgather(None, 16, 16, 1, 16, 16, 16, 16, None) == -1
+    assert lib.dbk_comm_open(0, 2, None, None, None) == -1
+    assert lib.dbk_comm_close(None) == -1
