@@ -235,7 +235,7 @@ class F2(Workload):
         Wg, Wu = self.W[self._e2e_i % self.nrep]
         self._e2e_i += 1
         self.x_dev.copy_(self.x_host, non_blocking=True)
-        h = self.ops.gateup_swiglu(self.x_dev, Wg, Wu)
+        h = self.ops.gateup_swiglu(self.x_dev, Wg, Wu, out=self.h_local)
         if self.world > 1:
             h = self.gather_blocks(h)
         self.out_host.copy_(h.reshape(-1), non_blocking=True)
@@ -308,7 +308,7 @@ class F1(F2):
         W = self.W[self._e2e_i % self.nrep]
         self._e2e_i += 1
         self.x_dev.copy_(self.x_host, non_blocking=True)
-        h = self.ops.rmsnorm_gemv(self.x_dev, self.gamma, W, eps=1e-6)
+        h = self.ops.rmsnorm_gemv(self.x_dev, self.gamma, W, eps=1e-6, out=self.h_local)
         if self.world > 1:
             h = self.gather_blocks(h)
         self.out_host.copy_(h.reshape(-1), non_blocking=True)
@@ -394,7 +394,7 @@ class F4(Workload):
         K, V = self.KV[self._e2e_i % self.nrep]
         self._e2e_i += 1
         self.q_dev.copy_(self.q_host, non_blocking=True)
-        o = self.ops.flashdecode(self.q_dev, K, V)
+        o = self.ops.flashdecode(self.q_dev, K, V, out=self.o)
         if self.world > 1:
             o = self.gather_blocks(o)
         self.out_host.copy_(o.reshape(-1), non_blocking=True)
@@ -501,7 +501,8 @@ class GQA(F4):
         K, V = self.KV[self._e2e_i % self.nrep]
         self._e2e_i += 1
         self.q_dev.copy_(self.q_host, non_blocking=True)
-        o = self.ops.flashdecode(self.q_dev, K, V, seq_lens=self.lens, page_table=self.table)
+        o = self.ops.flashdecode(self.q_dev, K, V, seq_lens=self.lens, page_table=self.table,
+                                 out=self.o)
         if self.world > 1:
             o = self.gather_rows(o.view(self.batch, -1))
         self.out_host.copy_(o.reshape(-1), non_blocking=True)
@@ -592,10 +593,11 @@ class MLP(Workload):
 
     def e2e_step(self):
         self.x_dev.copy_(self.x_host, non_blocking=True)
-        h = self.ops.gateup_swiglu(self.x_dev, self.Wg, self.Wu, gamma=self.gamma, eps=1e-5)
+        h = self.ops.gateup_swiglu(self.x_dev, self.Wg, self.Wu, gamma=self.gamma, eps=1e-5,
+                                   out=self.h)
         if self.world > 1:
             h = self.gather_rows(h)
-        y = self.ops.gemv(h, self.Wd)
+        y = self.ops.gemv(h, self.Wd, out=self.y)
         if self.world > 1:
             y = self.gather_rows(y)
         self.out_host.copy_(y.reshape(-1), non_blocking=True)
@@ -855,7 +857,7 @@ def main() -> int:
     e_us = e_ms * 1e3 / args.steps
     e2e = {"value": round(wl.step_bytes_total() / (e_us * 1e-6) / 1e9, 1), "unit": "GB/s",
            "us_per_step": round(e_us, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-           "path": "decodebench_b200.ops (ctypes -> libdbk.so C ABI), pinned host buffers"}
+           "path": "decodebench_b200.ops (ctypes -> libdbk.so C ABI), pinned host buffers, outputs preallocated (out=)"}
 
     line = None
     if rank == 0:

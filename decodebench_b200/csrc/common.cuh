@@ -55,7 +55,18 @@ extern __device__ unsigned long long dbk_trace[2048 * 16];
       dbk::dbk_trace[blockIdx.x * 16 + (slot)] = t_;                      \
     }                                                                     \
   } while (0)
+// Adds the time spent in a wait to dbk_trace[blockIdx.x * 16 + slot] (cond threads only).
+#define DBK_TIMED_WAIT(cond, slot, expr)                                  \
+  ([&]() {                                                                \
+    unsigned long long a_, b_;                                            \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(a_));                \
+    const bool r_ = (expr);                                               \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(b_));                \
+    if (cond) dbk::dbk_trace[blockIdx.x * 16 + (slot)] += b_ - a_;        \
+    return r_;                                                            \
+  }())
 #else
+#define DBK_TIMED_WAIT(cond, slot, expr) (expr)
 #define DBK_MARK(cond, slot) \
   do {                       \
   } while (0)

@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
       TileWalker w(a, tile0, u0);
       for (int u = u0, j = 0; u < u1; ++u, ++j, w.next()) {
         const int s = j % a.nstages;
-        if (j >= a.nstages && !mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty))
+        if (j >= a.nstages && !DBK_TIMED_WAIT(lane == 0, 10, mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty)))
           return;
         const int n = w.ntok();
         uint8_t* dk = smem + (size_t)s * kStage;
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
           const int j = g0 - u0 + i;
           const int s = j % a.nstages;
           if (j >= a.nstages &&
-              !mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty))
+              !DBK_TIMED_WAIT(lane == 0, 10, mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty)))
             gave_up = true;   // the error is recorded; leave after this group
           else {
             uint8_t* dk = smem + (size_t)s * kStage;
@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
     const uint32_t vst = kst + kStage / 2;
     if constexpr (kMma) {
       if ((j & 1) == grp) {
-        if (!mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull)) return;
+        if (!DBK_TIMED_WAIT(tid == 0, 11, mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull))) return;
         DBK_MARK(lane == 0 && warp == 0 && j == 0, 3);
         DBK_MARK(lane == 0 && warp == 0 && j == 16, 4);
         const int t0 = wi * 16;                 // this warp's 16 tokens
@@ -441,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
         if (lane == 0) mbar_arrive(&empty[s]);
       }
     } else {
-      if (!mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull)) return;
+      if (!DBK_TIMED_WAIT(tid == 0, 11, mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull))) return;
       const int mine = min(8, n - warp * 8);           // tokens of this warp
       if (mine > 0) {
         const uint32_t kbase = kst + (uint32_t)((warp * 8) * kD + 4 * lane) * sizeof(T);

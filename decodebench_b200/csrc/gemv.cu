@@ -59,6 +59,7 @@ struct GemvArgs {
   int slots;             // segments per stage (multiple of 8)
   int nstages;           // ring depth
   int max_rows;          // max output rows of any CTA
+  int pcols;             // tensor-core variant: B columns in use (batch, or 2 * batch packed)
 };
 
 // Shared-memory carve-up (dynamic): ring | full[] | empty[] | acc | inv_rms
@@ -275,7 +276,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(const GemvArgs
 //     sums the 8 warp partials in a fixed order (deterministic);
 //   * the activation is the B operand (N = 8 columns = the batch, up to 8):
 //     x * gamma is staged in shared memory as a high and a low 16-bit part and
-//     both are multiplied, so x * gamma keeps ~22 (fp16) / ~16 (bf16) bits;
+//     both are multiplied, so x * gamma keeps ~22 (fp16) / ~16 (bf16) bits.
+//     For batch <= 4 the two parts sit in different B columns of the same mma
+//     (columns b and batch + b), so the split costs no extra tensor-core work;
+//     the epilogue adds the two columns. For batch 5..8 a second mma multiplies
+//     the low parts;
 //   * SwiGLU: an m-tile holds 8 gate rows (rows 0..7) and the 8 up rows of the
 //     same outputs (rows 8..15), so the epilogue reads gate and up of an output
 //     from neighbouring partial rows.
@@ -293,8 +298,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)a.nstages * kMmaStage);
   uint64_t* empty = full + a.nstages;
   const int nmt_max = (a.max_rows + RPT - 1) / RPT;
-  float* part = reinterpret_cast<float*>(empty + a.nstages);   // [8 warps][nmt_max*16][batch]
-  uint16_t* xs_hi = reinterpret_cast<uint16_t*>(part + (size_t)kConsumerWarps * nmt_max * 16 * a.batch);
+  float* part = reinterpret_cast<float*>(empty + a.nstages);   // [8 warps][nmt_max*16][pcols]
+  const int pc = a.pcols;
+  uint16_t* xs_hi = reinterpret_cast<uint16_t*>(part + (size_t)kConsumerWarps * nmt_max * 16 * pc);
   uint16_t* xs_lo = xs_hi + (size_t)a.batch * a.d_in;
   __shared__ float red[kConsumerWarps][8];
   __shared__ float inv_rms[8];
@@ -306,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
   const int nrows = row1 - row0;
   const int nmt = (nrows + RPT - 1) / RPT;
   const int total = nmt * a.nchunks;
+  DBK_MARK(tid == 0, 0);
 
   if (tid == 0) {
     for (int s = 0; s < a.nstages; ++s) {
@@ -326,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
       for (int j = 0; j < total; ++j) {
         const int s = j % a.nstages;
         if (j >= a.nstages &&
-            !mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty))
+            !DBK_TIMED_WAIT(true, 10, mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty)))
           return;
         const int mt = j / a.nchunks, c = j - mt * a.nchunks;
         const int col0 = c * kMmaKC;
@@ -384,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
     }
   }
   named_bar_sync(1, kConsumers);
+  DBK_MARK(tid == 0, 1);
   if (tid < 8) {
     float v = 1.f;
     if (MODE != MODE_PLAIN && gam != nullptr && tid < a.batch) {
@@ -398,10 +406,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
   // column offset 8*(lane>>4) within a 16-column k-step.
   const int a_row = (lane & 7) + 8 * ((lane >> 3) & 1);
   const uint32_t a_lane_off = (uint32_t)(a_row * kMmaSlot + (8 * (lane >> 4)) * 2);
-  const int bn = lane >> 2;                  // B column (batch row) held by this lane
-  const bool b_ok = bn < a.batch;
-  const uint16_t* xh = xs_hi + (size_t)(b_ok ? bn : 0) * a.d_in + 2 * (lane & 3);
-  const uint16_t* xl = xs_lo + (size_t)(b_ok ? bn : 0) * a.d_in + 2 * (lane & 3);
+  const int bn = lane >> 2;                  // B column held by this lane
+  const bool packed = SPLIT && pc > a.batch;  // columns [batch, 2 batch) hold the low parts
+  const bool b_ok = bn < pc;
+  const uint16_t* xh =
+      (packed && bn >= a.batch ? xs_lo + (size_t)(bn - a.batch) * a.d_in
+                               : xs_hi + (size_t)(b_ok ? bn : 0) * a.d_in) + 2 * (lane & 3);
+  const uint16_t* xl = xs_lo + (size_t)(b_ok && bn < a.batch ? bn : 0) * a.d_in + 2 * (lane & 3);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
 
   for (int j = 0; j < total; ++j) {
@@ -409,7 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
     const int mt = j / a.nchunks, c = j - mt * a.nchunks;
     const int col0 = c * kMmaKC;
     const int seg = min(kMmaKC, a.d_in - col0);
-    if (!mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull)) return;
+    if (!DBK_TIMED_WAIT(tid == 0, 11, mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull))) return;
+    DBK_MARK(tid == 0 && j == 0, 2);
     const uint32_t stage = smem_u32(ring + (size_t)s * kMmaStage) + a_lane_off;
 #pragma unroll 4
     for (int kk = 0; kk < 16; ++kk) {
@@ -423,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
           b1 = *reinterpret_cast<const uint32_t*>(xh + col0 + k + 8);
         }
         Mma<T>::run(acc, af[0], af[1], af[2], af[3], b0, b1);
-        if constexpr (SPLIT) {
+        if (SPLIT && !packed) {
           uint32_t l0 = 0u, l1 = 0u;
           if (b_ok) {
             l0 = *reinterpret_cast<const uint32_t*>(xl + col0 + k);
@@ -438,19 +450,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
     if (c == a.nchunks - 1) {
       // m-tile done: accumulator rows (lane>>2) and (lane>>2)+8, columns 2*(lane&3) + {0,1}
       const int r = mt * 16 + (lane >> 2), n0 = 2 * (lane & 3);
-      float* pw = part + (size_t)warp * nmt_max * 16 * a.batch;
-      if (n0 < a.batch) {
-        pw[(size_t)r * a.batch + n0] = acc[0];
-        pw[(size_t)(r + 8) * a.batch + n0] = acc[2];
+      float* pw = part + (size_t)warp * nmt_max * 16 * pc;
+      if (n0 < pc) {
+        pw[(size_t)r * pc + n0] = acc[0];
+        pw[(size_t)(r + 8) * pc + n0] = acc[2];
       }
-      if (n0 + 1 < a.batch) {
-        pw[(size_t)r * a.batch + n0 + 1] = acc[1];
-        pw[(size_t)(r + 8) * a.batch + n0 + 1] = acc[3];
+      if (n0 + 1 < pc) {
+        pw[(size_t)r * pc + n0 + 1] = acc[1];
+        pw[(size_t)(r + 8) * pc + n0 + 1] = acc[3];
       }
       acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
     }
   }
   named_bar_sync(1, kConsumers);
+  DBK_MARK(tid == 0, 3);
 
   T* y = static_cast<T*>(a.y);
   const T* res = static_cast<const T*>(a.residual);
@@ -460,8 +473,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
     auto sum_row = [&](int slot) {
       float t = 0.f;
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w)
-        t += part[((size_t)w * nmt_max * 16 + mt * 16 + slot) * a.batch + b];
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float* pr = part + ((size_t)w * nmt_max * 16 + mt * 16 + slot) * pc;
+        t += packed ? pr[b] + pr[a.batch + b] : pr[b];
+      }
       return t;
     };
     float v;
@@ -477,6 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
     if (res != nullptr) v += Elem<T>::to_f(res[o]);
     y[o] = Elem<T>::from_f(v);
   }
+  DBK_MARK(tid == 0, 4);
 }
 
 // Shared-memory bytes of the tensor-core variant for a stage count (0 if it
@@ -484,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
 size_t mma_smem_bytes(const GemvArgs& a, int rpt, int nst) {
   if (a.d_in % 16 != 0 || a.batch > 8) return 0;
   const int nmt_max = (a.max_rows + rpt - 1) / rpt;
-  return (size_t)nst * (kMmaStage + 16) + (size_t)kConsumerWarps * nmt_max * 16 * a.batch * 4 +
+  return (size_t)nst * (kMmaStage + 16) + (size_t)kConsumerWarps * nmt_max * 16 * a.pcols * 4 +
          (size_t)a.batch * a.d_in * 4 + 256;
 }
 
@@ -535,6 +551,8 @@ int launch_t(const GemvArgs& a0, cudaStream_t st, const DeviceInfo& dev) {
     const int grid = a.d_out < dev.num_sms ? a.d_out : dev.num_sms;
     a.max_rows = (a.d_out + grid - 1) / grid;
     const int rpt = (MODE == MODE_SWIGLU) ? 8 : 16;
+    // x * gamma needs its low part; with batch <= 4 it rides in spare B columns
+    a.pcols = (a.gamma != nullptr && 2 * a.batch <= 8) ? 2 * a.batch : a.batch;
     for (int nst = kMmaStages; nst >= 2 && !simt_only; --nst) {
       const size_t smem = mma_smem_bytes(a, rpt, nst);
       if (smem != 0 && smem <= (size_t)dev.max_smem_optin - 1024) {

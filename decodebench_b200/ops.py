@@ -56,8 +56,26 @@ def workspace_bytes_flashdecode(batch: int, n_q_heads: int, n_kv_heads: int, max
                                                     split_tokens)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(dev: torch.device) -> int:
+    """The current CUDA stream of ``dev`` as a raw handle (no Stream object built)."""
+    if _raw_stream is not None:
+        return _raw_stream(dev.index)
     return torch.cuda.current_stream(dev).cuda_stream
+
+
+_ws_bytes_cache: dict[tuple, int] = {}
+
+
+def _ws_bytes(key: tuple, query) -> int:
+    """Workspace bytes of an op shape (a pure function of the shape: cached)."""
+    nb = _ws_bytes_cache.get(key)
+    if nb is None:
+        nb = int(query())
+        _ws_bytes_cache[key] = nb
+    return nb
 
 
 def _workspace(key: tuple, nbytes: int, device: torch.device,
@@ -100,9 +118,11 @@ def rmsnorm_gemv(x: torch.Tensor, gamma: torch.Tensor, W: torch.Tensor, eps: flo
         raise ValueError(f"shape mismatch: x {tuple(x.shape)}, gamma {tuple(gamma.shape)}, "
                          f"W {tuple(W.shape)}")
     y = out if out is not None else torch.empty(*x.shape[:-1], d_out, dtype=x.dtype, device=dev)
-    nb = N.load().dbk_workspace_bytes(N.DBK_OP_RMSNORM_GEMV, batch, d_in, d_out)
+    lib = N.load()
+    nb = _ws_bytes(("f1", batch, d_in, d_out),
+                   lambda: lib.dbk_workspace_bytes(N.DBK_OP_RMSNORM_GEMV, batch, d_in, d_out))
     ws = _workspace(("f1", batch, d_in, d_out), nb, dev, workspace)
-    N.check("dbk_rmsnorm_gemv", N.load().dbk_rmsnorm_gemv(
+    N.check("dbk_rmsnorm_gemv", lib.dbk_rmsnorm_gemv(
         x2.data_ptr(), gamma.data_ptr(), W.data_ptr(), y.data_ptr(), batch, d_in, d_out,
         float(eps), dt, _ptr(ws), nb, _stream(dev)))
     return y
@@ -124,9 +144,11 @@ def gateup_swiglu(x: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
     if Wg.dtype != x.dtype or Wu.dtype != x.dtype or (gamma is not None and gamma.dtype != x.dtype):
         raise TypeError("all operands must share one dtype")
     h = out if out is not None else torch.empty(*x.shape[:-1], d_ff, dtype=x.dtype, device=dev)
-    nb = N.load().dbk_workspace_bytes(N.DBK_OP_GATEUP_SWIGLU, batch, d_in, d_ff)
+    lib = N.load()
+    nb = _ws_bytes(("f2", batch, d_in, d_ff),
+                   lambda: lib.dbk_workspace_bytes(N.DBK_OP_GATEUP_SWIGLU, batch, d_in, d_ff))
     ws = _workspace(("f2", batch, d_in, d_ff), nb, dev, workspace)
-    N.check("dbk_gateup_swiglu", N.load().dbk_gateup_swiglu(
+    N.check("dbk_gateup_swiglu", lib.dbk_gateup_swiglu(
         x2.data_ptr(), _ptr(gamma), Wg.data_ptr(), Wu.data_ptr(), h.data_ptr(), batch, d_in,
         d_ff, float(eps), dt, _ptr(ws), nb, _stream(dev)))
     return h
@@ -145,9 +167,11 @@ def gemv(x: torch.Tensor, W: torch.Tensor, residual: torch.Tensor | None = None,
     if residual is not None and residual.numel() != batch * d_out:
         raise ValueError("residual must have the output's shape")
     y = out if out is not None else torch.empty(*x.shape[:-1], d_out, dtype=x.dtype, device=dev)
-    nb = N.load().dbk_workspace_bytes(N.DBK_OP_GEMV, batch, d_in, d_out)
+    lib = N.load()
+    nb = _ws_bytes(("gemv", batch, d_in, d_out),
+                   lambda: lib.dbk_workspace_bytes(N.DBK_OP_GEMV, batch, d_in, d_out))
     ws = _workspace(("gemv", batch, d_in, d_out), nb, dev, workspace)
-    N.check("dbk_gemv", N.load().dbk_gemv(
+    N.check("dbk_gemv", lib.dbk_gemv(
         x2.data_ptr(), W.data_ptr(), _ptr(residual), y.data_ptr(), batch, d_in, d_out, dt,
         _ptr(ws), nb, _stream(dev)))
     return y
@@ -197,7 +221,8 @@ def flashdecode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         scale = 1.0 / math.sqrt(d)
     o = out if out is not None else torch.empty_like(q)
     lib = N.load()
-    nb = lib.dbk_flashdecode_workspace_bytes(batch, hq, hkv, max_len, split_tokens)
+    nb = _ws_bytes(("f4", batch, hq, hkv, max_len, split_tokens),
+                   lambda: lib.dbk_flashdecode_workspace_bytes(batch, hq, hkv, max_len, split_tokens))
     ws = _workspace(("f4", batch, hq, hkv, max_len, split_tokens), nb, dev, workspace)
     N.check("dbk_flashdecode", lib.dbk_flashdecode(
         q3.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _ptr(page_table),
