@@ -74,7 +74,12 @@ size_t dbk_flashdecode_workspace_bytes(int batch, int n_q_heads, int n_kv_heads,
  * bench_variant.cu:379-387) and the Python stages rmsnorm + gemv
  * (src/decodebench/demos/llama_decode.py:36-43).
  * batch 1..8: streaming kernel (mma.sync; CUDA cores when d_in % 16 != 0), no workspace;
- * batch 9..256: tcgen05 tensor cores (needs workspace). */
+ * batch 9..256: tcgen05 tensor cores (needs workspace).
+ * Ordering (programmatic dependent launch, all GEMV entry points): W is
+ * streamed while the preceding kernel in the stream may still run; x, gamma
+ * and residual are read, and y written, after it has completed. Weights are
+ * not written during decode; if they are, by the immediately preceding dbk_*
+ * call, put an event between or set DBK_PDL=0. */
 int dbk_rmsnorm_gemv(const void* x, const void* gamma, const void* W, void* y,
                      int batch, int d_in, int d_out, float eps, int dtype,
                      void* workspace, size_t workspace_bytes, void* stream);
@@ -109,7 +114,14 @@ int dbk_gemv(const void* x, const void* W, const void* residual, void* y,
  *   split_tokens: tokens per split-KV work item (multiple of 64), 0 = automatic.
  * Replaces f4_partial_kernel + f4_reduce_kernel (validation/src/kernels/fused/f4.cu:173-319,
  * launched at bench_variant.cu:758-763) and the Python stages scores, softmax,
- * weighted_v (llama_decode.py:120-134). head_dim 128 only. */
+ * weighted_v (llama_decode.py:120-134). head_dim 128 only.
+ * Ordering (programmatic dependent launch): q is read, and out and the
+ * workspace are written, only after every earlier kernel in the stream has
+ * completed; seq_lens, the page table and the K/V cache are read earlier, while
+ * the preceding kernel may still run. This matters only when the preceding
+ * kernel is one of this library's (other kernels never release their
+ * dependents early): do not have the immediately preceding dbk_* call write
+ * them, or put an event / any other kernel between, or set DBK_PDL=0. */
 int dbk_flashdecode(const void* q, const void* k_cache, const void* v_cache,
                     const int32_t* page_table, const int32_t* seq_lens, void* out,
                     int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len,
