@@ -197,7 +197,7 @@ class F2(Workload):
         self.x_cpu = torch.randn(batch, d_in, generator=xg).half()
         self.x = self.x_cpu.to(dev)
         self.h_local = torch.empty(batch, self.rows, dtype=torch.float16, device=dev)
-        self.h_full = torch.empty(world, batch, self.rows, dtype=torch.float16, device=dev)
+        self.h_full = torch.empty(batch, world * self.rows, dtype=torch.float16, device=dev)
 
     def describe(self):
         return {"workload": f"F2 gate+up GEMV -> SwiGLU, x [{self.batch},{self.d_in}] fp16, "
@@ -215,13 +215,26 @@ class F2(Workload):
     def launch_bytes(self):
         return self.costs.gateup_swiglu_bytes(self.batch, self.d_in, self.rows)
 
+    exchanges_per_step = 0    # at N > 1 the all-gather runs inside the GEMV kernel
+
+    def xname(self) -> str:
+        return ("all-gather fused into the GEMV kernel (NVLink peer stores)"
+                if self.comm is not None else "NCCL all-gather")
+
+    def fused(self) -> bool:
+        """N > 1 with the peer exchange: the all-gather runs inside the GEMV kernel."""
+        return self.world > 1 and self.comm is not None and self.with_exchange
+
     def run_kernel(self, rep):
         Wg, Wu = self.W[rep % self.nrep]
-        self.ops.gateup_swiglu(self.x, Wg, Wu, out=self.h_local)
+        if self.fused():
+            self.ops.gateup_swiglu(self.x, Wg, Wu, out=self.h_full, comm=self.comm)
+        else:
+            self.ops.gateup_swiglu(self.x, Wg, Wu, out=self.h_local)
 
     def exchange(self):
-        if self.world > 1:
-            self.gather_blocks(self.h_local, self.h_full)
+        if self.world > 1 and not self.fused():
+            self.gather_rows(self.h_local, self.h_full)
 
     def e2e_setup(self):
         t = self.t
@@ -235,9 +248,12 @@ class F2(Workload):
         Wg, Wu = self.W[self._e2e_i % self.nrep]
         self._e2e_i += 1
         self.x_dev.copy_(self.x_host, non_blocking=True)
-        h = self.ops.gateup_swiglu(self.x_dev, Wg, Wu, out=self.h_local)
-        if self.world > 1:
-            h = self.gather_blocks(h)
+        if self.world > 1 and self.comm is not None:
+            h = self.ops.gateup_swiglu(self.x_dev, Wg, Wu, out=self.h_full, comm=self.comm)
+        else:
+            h = self.ops.gateup_swiglu(self.x_dev, Wg, Wu, out=self.h_local)
+            if self.world > 1:
+                h = self.gather_rows(h)
         self.out_host.copy_(h.reshape(-1), non_blocking=True)
 
     # reference CPU implementation (oracle/_ref: the reference's cpu_reference.cpp)
@@ -286,7 +302,7 @@ class F1(F2):
         self.g_cpu = torch.randn(d, generator=xg).half()
         self.x, self.gamma = self.x_cpu.to(dev), self.g_cpu.to(dev)
         self.h_local = torch.empty(1, self.rows, dtype=torch.float16, device=dev)
-        self.h_full = torch.empty(world, 1, self.rows, dtype=torch.float16, device=dev)
+        self.h_full = torch.empty(1, world * self.rows, dtype=torch.float16, device=dev)
 
     def describe(self):
         d = super().describe()
@@ -302,15 +318,23 @@ class F1(F2):
         return self.costs.rmsnorm_gemv_bytes(1, self.d_in, self.rows)
 
     def run_kernel(self, rep):
-        self.ops.rmsnorm_gemv(self.x, self.gamma, self.W[rep % self.nrep], eps=1e-6, out=self.h_local)
+        W = self.W[rep % self.nrep]
+        if self.fused():
+            self.ops.rmsnorm_gemv(self.x, self.gamma, W, eps=1e-6, out=self.h_full, comm=self.comm)
+        else:
+            self.ops.rmsnorm_gemv(self.x, self.gamma, W, eps=1e-6, out=self.h_local)
 
     def e2e_step(self):
         W = self.W[self._e2e_i % self.nrep]
         self._e2e_i += 1
         self.x_dev.copy_(self.x_host, non_blocking=True)
-        h = self.ops.rmsnorm_gemv(self.x_dev, self.gamma, W, eps=1e-6, out=self.h_local)
-        if self.world > 1:
-            h = self.gather_blocks(h)
+        if self.world > 1 and self.comm is not None:
+            h = self.ops.rmsnorm_gemv(self.x_dev, self.gamma, W, eps=1e-6, out=self.h_full,
+                                      comm=self.comm)
+        else:
+            h = self.ops.rmsnorm_gemv(self.x_dev, self.gamma, W, eps=1e-6, out=self.h_local)
+            if self.world > 1:
+                h = self.gather_rows(h)
         self.out_host.copy_(h.reshape(-1), non_blocking=True)
 
     def cpu_setup(self, frac_rows: float = 1.0):

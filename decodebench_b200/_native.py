@@ -13,6 +13,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libdbk.so"
 
 DBK_F16, DBK_BF16 = 0, 1
+DBK_ESHAPE = -2
 DBK_OP_RMSNORM_GEMV, DBK_OP_GATEUP_SWIGLU, DBK_OP_GEMV = 0, 1, 2
 
 # Every symbol include/dbk.h declares: name -> (restype, argtypes).
@@ -40,6 +41,9 @@ SIGNATURES = {
     "dbk_comm_close": (_I, [_P]),
     "dbk_comm_free": (_I, [_P]),
     "dbk_allgather": (_I, [_P, _P, _P, _I, _SZ, _SZ, _SZ, _SZ, _P]),
+    "dbk_rmsnorm_gemv_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P]),
+    "dbk_gateup_swiglu_allgather": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P]),
+    "dbk_gemv_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
 }
 
 DBK_COMM_RECORD_BYTES = 128

@@ -53,6 +53,13 @@ class PeerComm:
         self.capacity = int(capacity_bytes)
         dist.barrier(group=group)
 
+    @property
+    def handle(self):
+        """The ``dbk_comm*`` for the C-ABI entry points that take one."""
+        if not getattr(self, "_comm", None):
+            raise RuntimeError("PeerComm is closed")
+        return self._comm
+
     def _stream(self) -> int:
         return torch.cuda.current_stream(self.device).cuda_stream
 

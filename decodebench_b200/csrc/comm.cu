@@ -21,11 +21,7 @@
 // finished, which needs this rank's step e + 1 signal, which comes after this
 // rank's step e kernel has completed (stream order): the halves never race.
 //
-// Comm buffer of each rank (allocated by dbk_comm_alloc, zero-filled):
-//   [0, 8)         uint64 epoch   exchanges completed by this rank
-//   [8, 12)        uint32 arrive  CTAs of the running exchange that finished
-//   [256, +10 KB)  uint64 flag[8][160]  flag[p][c]: last exchange CTA c of rank p delivered
-//   [kHeader, ...) staging[2][world][capacity]
+// The comm buffer layout is in comm.cuh.
 //
 // No TMA and no multicast: only ordinary loads and stores, which is the only
 // kind of access to another GPU's memory this library makes.
@@ -35,16 +31,13 @@
 #include <cstring>
 #include <new>
 
+#include "comm.cuh"
 #include "common.cuh"
 #include "dbk_internal.h"
 
 namespace dbk {
 namespace {
 
-constexpr int kMaxWorld = 8;
-constexpr int kMaxCtas = 160;          // >= SMs per GPU: one flag slot per CTA
-constexpr size_t kFlags = 256;
-constexpr size_t kHeader = kFlags + (size_t)kMaxWorld * kMaxCtas * 8;   // 10496, 256-aligned
 constexpr int kAgThreads = 256;
 
 struct AgArgs {
@@ -55,24 +48,12 @@ struct AgArgs {
   int rank, world, rows, row_units;   // row_units = row_bytes / 16
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 
 __global__ void __launch_bounds__(kAgThreads) allgather_kernel(const AgArgs a) {
   DBK_MARK(threadIdx.x == 0, 6);
   asm volatile("griddepcontrol.wait;" ::: "memory");   // src comes from the previous kernel
   char* local = a.peer[a.rank];
-  auto* flags = reinterpret_cast<unsigned long long*>(local + kFlags);
-  auto* epoch_p = reinterpret_cast<unsigned long long*>(local);
-  auto* arrive = reinterpret_cast<unsigned int*>(local + 8);
-  const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(epoch_p);
+  const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(local);
   const int parity = (int)(e & 1);
   DBK_MARK(threadIdx.x == 0, 0);
   const long long units = (long long)a.rows * a.row_units;
@@ -93,11 +74,8 @@ __global__ void __launch_bounds__(kAgThreads) allgather_kernel(const AgArgs a) {
   DBK_MARK(threadIdx.x == 0, 1);
   __syncthreads();              // the CTA's stores happen before thread 0's release
   DBK_MARK(threadIdx.x == 0, 2);
-  if ((int)threadIdx.x < a.world && (int)threadIdx.x != a.rank) {
-    auto* slot = reinterpret_cast<unsigned long long*>(a.peer[threadIdx.x] + kFlags) +
-                 a.rank * kMaxCtas + blockIdx.x;
-    st_release_sys(slot, e + 1);   // release: cumulative over the CTA's stores (bar.sync above)
-  }
+  if ((int)threadIdx.x < a.world && (int)threadIdx.x != a.rank)   // release: cumulative over
+    st_release_sys(flag_slot(a.peer[threadIdx.x], a.rank, blockIdx.x), e + 1);  // the CTA's stores
 
   DBK_MARK(threadIdx.x == 0, 3);
   // 2. wait until every CTA slot of every peer holds this exchange's number
@@ -105,15 +83,7 @@ __global__ void __launch_bounds__(kAgThreads) allgather_kernel(const AgArgs a) {
   for (int t = threadIdx.x; t < nslots; t += blockDim.x) {
     const int p = t / (int)gridDim.x, c = t % (int)gridDim.x;
     if (p == a.rank) continue;
-    const unsigned long long* f = flags + p * kMaxCtas + c;
-    uint32_t n = 0;
-    while (ld_acquire_sys(f) < e + 1) {
-      if (++n >= kSpinLimit) {
-        record_error(kDevTimeoutPeer);
-        break;
-      }
-      __nanosleep(20);
-    }
+    wait_flag(flag_slot(local, p, c), e + 1);
   }
   __syncthreads();
   DBK_MARK(threadIdx.x == 0, 4);
@@ -133,13 +103,7 @@ __global__ void __launch_bounds__(kAgThreads) allgather_kernel(const AgArgs a) {
   // 4. the last CTA advances the sequence number (read by the next exchange
   //    after its griddepcontrol.wait, i.e. after this grid has completed)
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(arrive, 1u) == gridDim.x - 1) {
-      *arrive = 0;
-      *reinterpret_cast<volatile unsigned long long*>(epoch_p) = e + 1;
-    }
-  }
+  if (threadIdx.x == 0) finish_exchange(local, e);
   DBK_MARK(threadIdx.x == 0, 5);
   asm volatile("griddepcontrol.launch_dependents;");
 }
@@ -168,6 +132,19 @@ struct dbk_comm {
 };
 
 using dbk::PeerRecord;
+
+int dbk::comm_peerset(const dbk_comm* c, dbk::PeerSet* ps) {
+  if (!c || !ps) return DBK_ENULL;
+  int cur = -1;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return (int)e;
+  if (cur != c->device) return DBK_EDEVICE;
+  for (int p = 0; p < dbk::kMaxWorld; ++p) ps->peer[p] = p < c->world ? c->peer[p] : nullptr;
+  ps->capacity = (long long)c->capacity;
+  ps->rank = c->rank;
+  ps->world = c->world;
+  return DBK_OK;
+}
 
 extern "C" size_t dbk_comm_buffer_bytes(size_t capacity_per_rank, int world) {
   if (world < 1 || world > dbk::kMaxWorld) return 0;

@@ -26,6 +26,11 @@ int current_device_info(DeviceInfo* out);
 // device; later calls only check `smem` against the limit).
 int allow_dynamic_smem(const void* kern, const DeviceInfo& dev, size_t smem);
 
+struct PeerSet;   // comm.cuh
+// The peers of an open communicator, for kernels that fuse the all-gather
+// (DBK_EDEVICE unless the current device is the communicator's).
+int comm_peerset(const dbk_comm* c, PeerSet* ps);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Encode a 2-D tiled TMA descriptor over a row-major [rows, inner] matrix of

@@ -31,6 +31,7 @@
 // silu(g) = g / (1 + exp(-g)) (f2.cu:73), output rounded once to fp16/bf16.
 #include <cstdlib>
 
+#include "comm.cuh"
 #include "common.cuh"
 #include "dbk_internal.h"
 
@@ -60,6 +61,9 @@ struct GemvArgs {
   int nstages;           // ring depth
   int max_rows;          // max output rows of any CTA
   int pcols;             // tensor-core variant: B columns in use (batch, or 2 * batch packed)
+  long long y_ld;        // row stride of y and residual (elements)
+  long long y_col0;      // column of y (and residual) where this op's rows start
+  PeerSet ps;            // ps.world > 1: all-gather the output over the peers (fused)
 };
 
 // Shared-memory carve-up (dynamic): ring | full[] | empty[] | acc | inv_rms
@@ -252,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(const GemvArgs
     } else {
       v = sm.acc[(size_t)r * NB + b];
     }
-    const size_t o = (size_t)b * a.d_out + row0 + r;
+    const size_t o = (size_t)b * a.y_ld + a.y_col0 + row0 + r;
     if (res != nullptr) v += Elem<T>::to_f(res[o]);
     y[o] = Elem<T>::from_f(v);
   }
@@ -355,6 +359,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
 
   // -------------------------------------------------------------- consumers
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int ag_world = a.ps.world;
+  const unsigned long long ag_e =
+      ag_world > 1 ? *reinterpret_cast<volatile unsigned long long*>(a.ps.peer[a.ps.rank]) : 0ull;
+  const int ag_parity = (int)(ag_e & 1);
   const T* x = static_cast<const T*>(a.x);
   const T* gam = static_cast<const T*>(a.gamma);
   {
@@ -488,11 +496,39 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
     } else {
       v = sum_row(q);
     }
-    const size_t o = (size_t)b * a.d_out + row0 + r;
+    const size_t o = (size_t)b * a.y_ld + a.y_col0 + row0 + r;
     if (res != nullptr) v += Elem<T>::to_f(res[o]);
-    y[o] = Elem<T>::from_f(v);
+    const T out = Elem<T>::from_f(v);
+    y[o] = out;
+    // fused all-gather: the same value into every peer's staging block of this rank
+    for (int p = 0; p < ag_world; ++p)
+      if (p != a.ps.rank)
+        reinterpret_cast<T*>(staging(a.ps.peer[p], a.ps, ag_parity, a.ps.rank))
+            [(size_t)b * a.d_out + row0 + r] = out;
   }
   DBK_MARK(tid == 0, 4);
+  if (ag_world > 1) {
+    // Rows [row0, row1) of every rank's block come from the CTA with this index on
+    // that rank (same shape, same grid), so the CTA pairs up with its namesakes only.
+    char* local = a.ps.peer[a.ps.rank];
+    named_bar_sync(1, kConsumers);        // this CTA's stores precede the release below
+    if (tid < ag_world && tid != a.ps.rank) {
+      st_release_sys(flag_slot(a.ps.peer[tid], a.ps.rank, blockIdx.x), ag_e + 1);
+      wait_flag(flag_slot(local, tid, blockIdx.x), ag_e + 1);
+    }
+    named_bar_sync(1, kConsumers);
+    for (int idx = tid; idx < (ag_world - 1) * nrows * a.batch; idx += kConsumers) {
+      const int q = idx / (nrows * a.batch), rem = idx - q * nrows * a.batch;
+      const int p = q + (q >= a.ps.rank ? 1 : 0);
+      const int b = rem / nrows, r = rem - b * nrows;
+      const T* st = reinterpret_cast<const T*>(staging(local, a.ps, ag_parity, p));
+      const unsigned short u =
+          __ldcg(reinterpret_cast<const unsigned short*>(st) + (size_t)b * a.d_out + row0 + r);
+      reinterpret_cast<unsigned short*>(y)[(size_t)b * a.y_ld + (size_t)p * a.d_out + row0 + r] = u;
+    }
+    named_bar_sync(1, kConsumers);
+    if (tid == 0) finish_exchange(local, ag_e);
+  }
 }
 
 // Shared-memory bytes of the tensor-core variant for a stage count (0 if it
@@ -561,6 +597,7 @@ int launch_t(const GemvArgs& a0, cudaStream_t st, const DeviceInfo& dev) {
       }
     }
   }
+  if (a.ps.world > 1) return DBK_ESHAPE;   // the fused all-gather needs the tensor-core variant
   if (a.batch <= 1) return launch_nb<T, 1, MODE>(a, st, dev);
   if (a.batch <= 2) return launch_nb<T, 2, MODE>(a, st, dev);
   if (a.batch <= 4) return launch_nb<T, 4, MODE>(a, st, dev);
@@ -571,6 +608,7 @@ int gemv_dispatch(int mode, GemvArgs a, int dtype, cudaStream_t st) {
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc) return rc;
+  if (a.y_ld == 0) a.y_ld = a.d_out;
   if (dtype == DBK_F16) {
     switch (mode) {
       case MODE_PLAIN: return launch_t<__half, MODE_PLAIN>(a, st, dev);
@@ -644,4 +682,66 @@ extern "C" int dbk_gemv(const void* x, const void* W, const void* residual, void
   a.x = x; a.w0 = W; a.residual = residual; a.y = y;
   a.batch = batch; a.d_in = d_in; a.d_out = d_out;
   return gemv_dispatch(MODE_PLAIN, a, dtype, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------
+// Sharded GEMV with the shard-boundary all-gather fused into the epilogue
+// (batch 1..8). Each rank computes d_local output columns; every CTA stores its
+// rows into the peers' staging blocks as it produces them, publishes a release
+// flag, waits (bounded) for the same-index CTA of each peer and copies their
+// rows into y_full [batch][world * d_local] (rank p's columns start at
+// p * d_local). No separate collective launch.
+namespace {
+
+int gemv_ag(int mode, dbk_comm* comm, GemvArgs a, int dtype, void* stream) {
+  if (!comm) return DBK_ENULL;
+  if (a.batch > kSimtMaxBatch) return DBK_ESHAPE;
+  PeerSet ps;
+  if (int rc = comm_peerset(comm, &ps)) return rc;
+  if ((long long)a.batch * a.d_out * 2 > ps.capacity) return DBK_EWORKSPACE;
+  a.ps = ps;
+  a.y_ld = (long long)ps.world * a.d_out;
+  a.y_col0 = (long long)ps.rank * a.d_out;
+  if (ps.world == 1) a.ps.world = 0;   // nothing to exchange
+  return gemv_dispatch(mode, a, dtype, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+extern "C" int dbk_rmsnorm_gemv_allgather(dbk_comm* comm, const void* x, const void* gamma,
+                                          const void* W, void* y_full, int batch, int d_in,
+                                          int d_local, float eps, int dtype, void* stream) {
+  int rc = check_common(x, W, y_full, batch, d_in, d_local, dtype);
+  if (rc) return rc;
+  if (!gamma) return DBK_ENULL;
+  if (!aligned16(gamma)) return DBK_EALIGN;
+  GemvArgs a{};
+  a.x = x; a.gamma = gamma; a.w0 = W; a.y = y_full;
+  a.batch = batch; a.d_in = d_in; a.d_out = d_local; a.eps = eps;
+  return gemv_ag(MODE_NORM, comm, a, dtype, stream);
+}
+
+extern "C" int dbk_gateup_swiglu_allgather(dbk_comm* comm, const void* x, const void* gamma,
+                                           const void* Wg, const void* Wu, void* h_full,
+                                           int batch, int d_in, int d_local, float eps,
+                                           int dtype, void* stream) {
+  int rc = check_common(x, Wg, h_full, batch, d_in, d_local, dtype);
+  if (rc) return rc;
+  if (!Wu) return DBK_ENULL;
+  if (!aligned16(Wu) || (gamma && !aligned16(gamma))) return DBK_EALIGN;
+  GemvArgs a{};
+  a.x = x; a.gamma = gamma; a.w0 = Wg; a.w1 = Wu; a.y = h_full;
+  a.batch = batch; a.d_in = d_in; a.d_out = d_local; a.eps = eps;
+  return gemv_ag(MODE_SWIGLU, comm, a, dtype, stream);
+}
+
+extern "C" int dbk_gemv_allgather(dbk_comm* comm, const void* x, const void* W,
+                                  const void* residual_full, void* y_full, int batch, int d_in,
+                                  int d_local, int dtype, void* stream) {
+  int rc = check_common(x, W, y_full, batch, d_in, d_local, dtype);
+  if (rc) return rc;
+  GemvArgs a{};
+  a.x = x; a.w0 = W; a.residual = residual_full; a.y = y_full;
+  a.batch = batch; a.d_in = d_in; a.d_out = d_local;
+  return gemv_ag(MODE_PLAIN, comm, a, dtype, stream);
 }

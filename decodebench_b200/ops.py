@@ -103,10 +103,41 @@ def _workspace(key: tuple, nbytes: int, device: torch.device,
         return ws
 
 
+def _sharded(name: str, comm, x2: torch.Tensor, d_local: int, out, fused_call, local_call):
+    """Column-sharded op followed by the all-gather: [batch, world * d_local].
+
+    ``fused_call(y_full)`` runs the kernel with the exchange in its epilogue; a
+    DBK_ESHAPE answer (shape outside the fused variant) falls back to the local
+    op plus ``comm.all_gather_rows``."""
+    batch = x2.shape[0]
+    y = out if out is not None else torch.empty(batch, comm.world * d_local, dtype=x2.dtype,
+                                                device=x2.device)
+    if tuple(y.shape) != (batch, comm.world * d_local) or not y.is_contiguous():
+        raise ValueError(f"out must be contiguous [{batch}, {comm.world * d_local}]")
+    st = fused_call(y)
+    if st == N.DBK_ESHAPE:
+        return comm.all_gather_rows(local_call(), y)
+    N.check(name, st)
+    return y
+
+
 def rmsnorm_gemv(x: torch.Tensor, gamma: torch.Tensor, W: torch.Tensor, eps: float = 1e-6,
                  out: torch.Tensor | None = None,
-                 workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """F1: ``linear(rmsnorm(x) * gamma, W)`` for x [batch, d_in], W [d_out, d_in]."""
+                 workspace: torch.Tensor | None = None, comm=None) -> torch.Tensor:
+    """F1: ``linear(rmsnorm(x) * gamma, W)`` for x [batch, d_in], W [d_out, d_in].
+
+    With ``comm`` (a :class:`decodebench_b200.comm.PeerComm`), W holds this rank's
+    d_out rows and the result is all-gathered over the ranks inside the kernel:
+    [batch, world * d_out], rank p's columns at p * d_out."""
+    if comm is not None and comm.world > 1:
+        _need_cuda(x, gamma, W, out)
+        x2 = x.reshape(-1, x.shape[-1])
+        return _sharded("dbk_rmsnorm_gemv_allgather", comm, x2, W.shape[0], out,
+                        lambda y: N.load().dbk_rmsnorm_gemv_allgather(
+                            comm.handle, x2.data_ptr(), gamma.data_ptr(), W.data_ptr(),
+                            y.data_ptr(), x2.shape[0], x2.shape[1], W.shape[0], float(eps),
+                            _dtype_code(x), _stream(x.device)),
+                        lambda: rmsnorm_gemv(x2, gamma, W, eps=eps, workspace=workspace))
     dev = _need_cuda(x, gamma, W, out)
     dt = _dtype_code(x)
     if gamma.dtype != x.dtype or W.dtype != x.dtype:
@@ -131,8 +162,21 @@ def rmsnorm_gemv(x: torch.Tensor, gamma: torch.Tensor, W: torch.Tensor, eps: flo
 def gateup_swiglu(x: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
                   gamma: torch.Tensor | None = None, eps: float = 1e-6,
                   out: torch.Tensor | None = None,
-                  workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """F2: ``silu(x Wg^T) * (x Wu^T)``; with ``gamma``, x is RMS-normalised first."""
+                  workspace: torch.Tensor | None = None, comm=None) -> torch.Tensor:
+    """F2: ``silu(x Wg^T) * (x Wu^T)``; with ``gamma``, x is RMS-normalised first.
+
+    With ``comm``, Wg/Wu hold this rank's rows and the result is all-gathered
+    inside the kernel ([batch, world * d_ff_local], as rmsnorm_gemv)."""
+    if comm is not None and comm.world > 1:
+        _need_cuda(x, Wg, Wu, gamma, out)
+        x2 = x.reshape(-1, x.shape[-1])
+        return _sharded("dbk_gateup_swiglu_allgather", comm, x2, Wg.shape[0], out,
+                        lambda y: N.load().dbk_gateup_swiglu_allgather(
+                            comm.handle, x2.data_ptr(), _ptr(gamma), Wg.data_ptr(),
+                            Wu.data_ptr(), y.data_ptr(), x2.shape[0], x2.shape[1], Wg.shape[0],
+                            float(eps), _dtype_code(x), _stream(x.device)),
+                        lambda: gateup_swiglu(x2, Wg, Wu, gamma=gamma, eps=eps,
+                                              workspace=workspace))
     dev = _need_cuda(x, Wg, Wu, gamma, out)
     dt = _dtype_code(x)
     x2 = x.reshape(-1, x.shape[-1])
@@ -155,8 +199,29 @@ def gateup_swiglu(x: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
 
 
 def gemv(x: torch.Tensor, W: torch.Tensor, residual: torch.Tensor | None = None,
-         out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """``linear(x, W) (+ residual)`` for x [batch, d_in], W [d_out, d_in]."""
+         out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+         comm=None) -> torch.Tensor:
+    """``linear(x, W) (+ residual)`` for x [batch, d_in], W [d_out, d_in].
+
+    With ``comm``, W holds this rank's rows, ``residual`` (optional) is the full
+    [batch, world * d_out] tensor, and the result is all-gathered inside the kernel."""
+    if comm is not None and comm.world > 1:
+        _need_cuda(x, W, residual, out)
+        x2 = x.reshape(-1, x.shape[-1])
+        d_local = W.shape[0]
+
+        def local():
+            r = None
+            if residual is not None:
+                r = residual.reshape(x2.shape[0], -1)[:, comm.rank * d_local:(comm.rank + 1) * d_local]
+                r = r.contiguous()
+            return gemv(x2, W, residual=r, workspace=workspace)
+        return _sharded("dbk_gemv_allgather", comm, x2, d_local, out,
+                        lambda y: N.load().dbk_gemv_allgather(
+                            comm.handle, x2.data_ptr(), W.data_ptr(), _ptr(residual),
+                            y.data_ptr(), x2.shape[0], x2.shape[1], d_local, _dtype_code(x),
+                            _stream(x.device)),
+                        local)
     dev = _need_cuda(x, W, residual, out)
     dt = _dtype_code(x)
     x2 = x.reshape(-1, x.shape[-1])

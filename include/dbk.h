@@ -186,6 +186,29 @@ int dbk_comm_free(void* buf);
 int dbk_allgather(dbk_comm* comm, const void* src, void* out, int rows, size_t row_bytes,
                   size_t src_ld, size_t out_ld, size_t out_block, void* stream);
 
+/* Sharded GEMVs with the all-gather fused in (batch 1..8, one process per GPU).
+ * Each rank holds d_local rows of the weights (its output columns) and writes
+ * the gathered result y_full [batch][world * d_local] on every rank, rank p's
+ * columns at [p * d_local, (p + 1) * d_local). The exchange happens inside the
+ * GEMV kernel: every CTA stores its output rows straight into the peers' comm
+ * buffers, then waits (bounded) only for the CTA with the same index on each
+ * peer. Replaces "dbk_rmsnorm_gemv / dbk_gateup_swiglu / dbk_gemv followed by
+ * ncclAllGather" in a column-sharded decode (no counterpart in the single-GPU
+ * reference). residual_full (may be NULL) has y_full's layout; the local
+ * columns are read. Same argument rules as the unsharded entry points, plus
+ * batch * d_local * elem_size <= the comm's capacity; DBK_ESHAPE when the
+ * shape needs the CUDA-core variant (d_in % 16 != 0) or batch > 8. Every rank
+ * must make the same calls in the same order, interleaved in the same way with
+ * dbk_allgather. */
+int dbk_rmsnorm_gemv_allgather(dbk_comm* comm, const void* x, const void* gamma, const void* W,
+                               void* y_full, int batch, int d_in, int d_local, float eps,
+                               int dtype, void* stream);
+int dbk_gateup_swiglu_allgather(dbk_comm* comm, const void* x, const void* gamma,
+                                const void* Wg, const void* Wu, void* h_full, int batch,
+                                int d_in, int d_local, float eps, int dtype, void* stream);
+int dbk_gemv_allgather(dbk_comm* comm, const void* x, const void* W, const void* residual_full,
+                       void* y_full, int batch, int d_in, int d_local, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

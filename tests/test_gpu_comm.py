@@ -1,4 +1,5 @@
-"""dbk_allgather (NVLink peer-store all-gather) against NCCL's all-gather on 2 GPUs.
+"""dbk_allgather (NVLink peer-store all-gather) and the GEMVs with the all-gather
+fused in (dbk_*_allgather) against NCCL's all-gather on 2 GPUs.
 
 Two processes, one per GPU (the exchange waits on the other rank, so both ranks
 must own a GPU each; the test is skipped with fewer than 2 GPUs). Checked:
@@ -75,6 +76,54 @@ def _worker(rank: int, world: int, port: int, errq):
             dist.all_gather_into_tensor(full, src)
             assert torch.equal(out, full.permute(1, 0, 2).reshape(4, world * 1024)), \
                 f"graph replay {it} differs"
+        # GEMVs with the all-gather fused into the kernel, against the same op
+        # unfused + NCCL (bit-identical: same kernel arithmetic per CTA)
+        def nccl_rows(t):
+            full = torch.empty(world, *t.shape, dtype=t.dtype, device=dev)
+            dist.all_gather_into_tensor(full, t.contiguous())
+            return full.permute(1, 0, 2).reshape(t.shape[0], world * t.shape[1])
+
+        for it in range(3):
+            for dt, batch, d_in, d_loc in ((torch.float16, 1, 1024, 688),
+                                           (torch.bfloat16, 3, 2048, 512),
+                                           (torch.float16, 8, 512, 200)):
+                x = torch.randn(batch, d_in, generator=g, device=dev).to(dt)
+                gam = torch.randn(d_in, generator=g, device=dev).to(dt)
+                Wg = (torch.randn(d_loc, d_in, generator=g, device=dev) / 32).to(dt)
+                Wu = (torch.randn(d_loc, d_in, generator=g, device=dev) / 32).to(dt)
+                got = ops.gateup_swiglu(x, Wg, Wu, gamma=gam, eps=1e-5, comm=comm)
+                ref = nccl_rows(ops.gateup_swiglu(x, Wg, Wu, gamma=gam, eps=1e-5))
+                assert torch.equal(got, ref), f"fused F2 differs ({dt}, batch {batch}, it {it})"
+                got = ops.rmsnorm_gemv(x, gam, Wg, eps=1e-6, comm=comm)
+                ref = nccl_rows(ops.rmsnorm_gemv(x, gam, Wg, eps=1e-6))
+                assert torch.equal(got, ref), f"fused F1 differs ({dt}, batch {batch}, it {it})"
+                res = torch.randn(batch, world * d_loc, generator=g, device=dev).to(dt)
+                dist.broadcast(res, 0)
+                got = ops.gemv(x, Wu, residual=res, comm=comm)
+                loc = res[:, rank * d_loc:(rank + 1) * d_loc].contiguous()
+                ref = nccl_rows(ops.gemv(x, Wu, residual=loc))
+                assert torch.equal(got, ref), f"fused GEMV differs ({dt}, batch {batch}, it {it})"
+                # the standalone exchange interleaved with the fused ones
+                got = comm.all_gather_rows(x)
+                assert torch.equal(got, nccl_rows(x))
+        # fused op inside a CUDA graph
+        x = torch.zeros(1, 1024, dtype=torch.float16, device=dev)
+        Wg = (torch.randn(344, 1024, generator=g, device=dev) / 32).half()
+        Wu = (torch.randn(344, 1024, generator=g, device=dev) / 32).half()
+        h = torch.empty(1, world * 344, dtype=torch.float16, device=dev)
+        with torch.cuda.stream(s):
+            ops.gateup_swiglu(x, Wg, Wu, out=h, comm=comm)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ops.gateup_swiglu(x, Wg, Wu, out=h, comm=comm)
+        for it in range(3):
+            x.copy_(torch.randn(1, 1024, generator=g, device=dev).half())
+            dist.broadcast(x, 0)
+            graph.replay()
+            ref = nccl_rows(ops.gateup_swiglu(x, Wg, Wu))
+            assert torch.equal(h, ref), f"fused graph replay {it} differs"
         torch.cuda.synchronize()
         assert ops.take_device_error() == 0, "a bounded wait gave up"
         dist.barrier()
