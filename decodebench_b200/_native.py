@@ -44,6 +44,7 @@ SIGNATURES = {
     "dbk_rmsnorm_gemv_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P]),
     "dbk_gateup_swiglu_allgather": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P]),
     "dbk_gemv_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "dbk_copy": (_I, [_P, _P, _SZ, _P]),
 }
 
 DBK_COMM_RECORD_BYTES = 128

@@ -296,6 +296,32 @@ def flashdecode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     return o
 
 
+def stage(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    """Copy a decode step's input in, or its result out, with a small kernel.
+
+    One side is a CUDA tensor, the other a pinned CPU tensor (or CUDA too); both
+    contiguous with the same byte size. Runs on the CUDA side's current stream,
+    like ``dst.copy_(src, non_blocking=True)``, but without a copy-engine
+    transfer's fixed latency, and a following decode kernel can start streaming
+    its weights while the input arrives. Read a host ``dst`` only after the
+    stream has completed."""
+    dev = dst.device if dst.is_cuda else src.device
+    if dev.type != "cuda":
+        raise RuntimeError("stage: one side must be a CUDA tensor")
+    if not (dst.is_contiguous() and src.is_contiguous()):
+        raise ValueError("stage: tensors must be contiguous")
+    nb = dst.numel() * dst.element_size()
+    if nb != src.numel() * src.element_size():
+        raise ValueError("stage: byte sizes differ")
+    st = N.load().dbk_copy(dst.data_ptr(), src.data_ptr(), nb, _stream(dev))
+    if st != 0:
+        for t in (dst, src):     # the usual cause: pageable host memory
+            if not t.is_cuda and not t.is_pinned():
+                raise ValueError("stage: a CPU tensor must be pinned (pin_memory())")
+        N.check("dbk_copy", st)
+    return dst
+
+
 def take_device_error() -> int:
     """Error code a kernel recorded after a bounded wait gave up (0 = none); clears it."""
     return N.load().dbk_take_device_error()

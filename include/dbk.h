@@ -209,6 +209,17 @@ int dbk_gateup_swiglu_allgather(dbk_comm* comm, const void* x, const void* gamma
 int dbk_gemv_allgather(dbk_comm* comm, const void* x, const void* W, const void* residual_full,
                        void* y_full, int batch, int d_in, int d_local, int dtype, void* stream);
 
+/* Stream-ordered copy by a kernel, for a decode step's small inputs and outputs
+ * (a few KB): dst and src may each be device memory or pinned host memory
+ * (cudaHostAlloc / torch pin_memory, reached through its unified address), not
+ * pageable memory (DBK_EDEVICE). Both 16-byte aligned (DBK_EALIGN otherwise).
+ * Lower fixed latency than a copy-engine transfer at these sizes, and it keeps
+ * the programmatic-dependent-launch chain: a following library kernel starts
+ * streaming its weights while the input is still arriving. A copy into host
+ * memory is visible to the host once the stream's work has completed. No
+ * counterpart in the reference (whose harness uses cudaMemcpy). */
+int dbk_copy(void* dst, const void* src, size_t bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

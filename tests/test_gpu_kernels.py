@@ -266,3 +266,28 @@ def test_argument_errors(ops):
     K = torch.zeros(1, 2, 64, 128, dtype=torch.float16, device="cuda")
     with pytest.raises(DbkError):
         ops.flashdecode(q, K, K)   # 3 q heads over 2 kv heads
+
+
+@pytest.mark.gpu
+def test_stage_copies_between_pinned_host_and_device():
+    """ops.stage (dbk_copy): pinned host -> device and back, bit-exact, including
+    sizes that are not a multiple of 16 bytes; pageable memory is refused."""
+    import torch
+
+    from decodebench_b200 import ops
+    from decodebench_b200._native import DbkError
+
+    for n in (8, 4096, 11008, 1000003):
+        src = torch.randint(-30000, 30000, (n,), dtype=torch.int16).pin_memory()
+        dev = torch.empty(n, dtype=torch.int16, device="cuda")
+        back = torch.empty(n, dtype=torch.int16).pin_memory()
+        ops.stage(dev, src)
+        ops.stage(back, dev)
+        torch.cuda.synchronize()
+        assert torch.equal(back, src), f"round trip differs at {n} elements"
+        assert torch.equal(dev.cpu(), src)
+    with pytest.raises(ValueError):
+        ops.stage(torch.empty(16, dtype=torch.int16, device="cuda"), torch.zeros(16, dtype=torch.int16))
+    with pytest.raises(DbkError):
+        big = torch.empty(17, dtype=torch.int8, device="cuda")
+        ops.stage(big[1:], torch.zeros(16, dtype=torch.int8).pin_memory())   # misaligned
