@@ -25,6 +25,7 @@ enum DeviceError : int {
   kDevTimeoutMma = 3,       // waited too long for a tensor-core commit
   kDevTimeoutDrain = 4,     // waited too long for in-flight copies at exit
   kDevTimeoutPeer = 5,      // waited too long for another GPU's all-gather signal
+  kDevTimeoutMerge = 6,     // waited too long for the other contributors of a tile
 };
 
 extern __device__ int dbk_device_error;
@@ -36,6 +37,12 @@ constexpr uint32_t kSpinLimit = 1u << 24;
 
 __device__ __forceinline__ void record_error(int code) {
   atomicCAS(&dbk_device_error, 0, code);
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

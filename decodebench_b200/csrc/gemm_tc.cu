@@ -52,6 +52,9 @@ constexpr int kBN = 256;        // weight rows per tile (the MMA N)
 constexpr int kBK = 64;         // k-block (one 128-byte swizzle atom of 16-bit values)
 constexpr int kTcThreads = 192; // producer, MMA, 4 epilogue warps
 constexpr int kMaxRows = 128;   // A rows per pass (hi + lo rows when split)
+// Tiles with at most this many contributing CTAs are merged at once by the last
+// to arrive; tiles with more are merged by all contributors together at the end.
+constexpr int kLocalMerge = 4;
 
 struct TcArgs {
   CUtensorMap wmap0;   // W (or Wg) [d_out, d_in], box [256 rows x 64]
@@ -61,7 +64,7 @@ struct TcArgs {
   void* y;                // [batch, d_out]
   const float* inv_rms;   // [NB] (NORM / SWIGLU with gamma) or nullptr
   float* part;            // [2 * grid][NACC][batch][256] fp32 partials
-  int* done;              // [n-tiles] arrival counters (zero between launches)
+  int* done;              // [2][n-tiles] arrival / departure counters (zero between launches)
   int batch, nb, rows;    // batch, its padding to 8 (lo rows start at nb), A rows loaded
   int d_in, d_out;
   int ntiles, kblocks;
@@ -190,9 +193,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   uint64_t* acc_full = empty + a.nstages;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* teardown = acc_empty + 1;
+  uint64_t* mrg_bar = teardown + 1;            // merge copies (the ring is idle by then)
   __shared__ uint32_t s_tmem;
-  __shared__ int s_last;
   __shared__ volatile int s_bail;
+  __shared__ int s_last;
   __shared__ float xbuf[kMaxRows / 2][17];    // lo-row exchange (split)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -210,6 +214,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 4);
     mbar_init(teardown, kTcThreads / 32);
+    mbar_init(mrg_bar, 1);
     fence_barrier_init();
     s_bail = 0;
   }
@@ -333,6 +338,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         named_bar_sync(1, 128);
       }
     };
+    // Epilogue of batch row b, weight rows col0 + gq*16 .. +15.
+    auto finish_row = [&](int col0, int b, int gq, const float (&g0)[16], const float (&g1)[16]) {
+      const float scb = a.inv_rms ? a.inv_rms[b] : 1.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int c = col0 + gq * 16 + i;
+        if (c >= a.d_out) break;
+        float val;
+        if constexpr (MODE == TC_SWIGLU) val = silu(g0[i] * scb) * (g1[i] * scb);
+        else if constexpr (MODE == TC_NORM) val = g0[i] * scb;
+        else val = g0[i];
+        const size_t o = (size_t)b * a.d_out + c;
+        if (res != nullptr) val += Elem<T>::to_f(res[o]);
+        y[o] = Elem<T>::from_f(val);
+      }
+    };
+    int pend[2];                                  // partial tiles of this CTA (<= 2)
+    int npend = 0;
+    uint32_t mphase = 0;                          // parity of mrg_bar
     int seg = 0;
     for (int j0 = 0; active && j0 < u1 - u0 && !s_bail;) {
       const int u = u0 + j0, nt = u / a.kblocks, kb0 = u - nt * a.kblocks;
@@ -342,25 +366,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       DBK_MARK(etid == 0, seg == 0 ? 6 : 11);
       const bool whole = (kb0 == 0) && (len == a.kblocks);
       const int col0 = nt * kBN;
-      // Epilogue of batch row b, weight rows col0 + gq*16 .. +15.
-      auto finish_row = [&](int b, int gq, const float (&g0)[16], const float (&g1)[16]) {
-        const float scb = a.inv_rms ? a.inv_rms[b] : 1.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int c = col0 + gq * 16 + i;
-          if (c >= a.d_out) break;
-          float val;
-          if constexpr (MODE == TC_SWIGLU) val = silu(g0[i] * scb) * (g1[i] * scb);
-          else if constexpr (MODE == TC_NORM) val = g0[i] * scb;
-          else val = g0[i];
-          const size_t o = (size_t)b * a.d_out + c;
-          if (res != nullptr) val += Elem<T>::to_f(res[o]);
-          y[o] = Elem<T>::from_f(val);
-        }
-      };
       auto finish = [&](int gq, const float (&g0)[16], const float (&g1)[16]) {
-        if (owner_row) finish_row(r, gq, g0, g1);
+        if (owner_row) finish_row(col0, r, gq, g0, g1);
       };
+
       if (whole) {
         for (int gq = 0; gq < kBN / 16; ++gq) {
           float g0[16], g1[16];
@@ -397,30 +406,36 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       named_bar_sync(1, 128);
       const int first_u = nt * a.kblocks, last_u = first_u + a.kblocks - 1;
       const int c_first = owner(first_u, U, G), c_last = owner(last_u, U, G);
-      if (etid == 0) {
-        const int prev = atomicAdd(&a.done[nt], 1);
-        s_last = (prev == c_last - c_first);
+      if (c_last - c_first + 1 > kLocalMerge) {
+        // Arrive at once; the merge runs after the last segment (an arrival never
+        // waits on a merge, so no CTA waits on a chain of its neighbours).
+        if (etid == 0) atomicAdd(&a.done[nt], 1);
+        if (npend < 2) pend[npend++] = nt;
+        j0 += len;
+        ++seg;
+        continue;
       }
+      // Few contributors: the last to arrive merges the whole tile now.
+      if (etid == 0) s_last = (atomicAdd(&a.done[nt], 1) == c_last - c_first);
       named_bar_sync(1, 128);
       const bool last = s_last != 0;
       named_bar_sync(1, 128);                   // s_last is rewritten by the next segment
       if (last) {
         __threadfence();
-        // All 128 epilogue threads share the merge: item = (batch row, 16 columns).
         for (int it = etid; it < a.batch * (kBN / 16); it += 128) {
           const int b = it / (kBN / 16), gq = it - b * (kBN / 16);
           float g0[16], g1[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) g0[i] = g1[i] = 0.f;
-#pragma unroll 2
           for (int c = c_first; c <= c_last; ++c) {
             const int sl = 2 * c + (range_start(c, U, G) >= first_u ? 0 : 1);
 #pragma unroll
             for (int acc = 0; acc < NACC; ++acc) {
-              const float* src = a.part + (((size_t)sl * NACC + acc) * a.batch + b) * kBN + gq * 16;
+              const float4* src = reinterpret_cast<const float4*>(
+                  a.part + (((size_t)sl * NACC + acc) * a.batch + b) * kBN + gq * 16);
               float4 p4[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) p4[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
+              for (int i = 0; i < 4; ++i) p4[i] = __ldcg(src + i);
               float* g = acc ? g1 : g0;
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
@@ -429,12 +444,91 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
               }
             }
           }
-          finish_row(b, gq, g0, g1);
+          finish_row(col0, b, gq, g0, g1);
         }
         if (etid == 0) a.done[nt] = 0;        // ready for the next launch
       }
       j0 += len;
       ++seg;
+    }
+    // Merges of the partial tiles: every contributor waits (bounded) until all
+    // contributors have arrived, then merges its own slice of the tile's outputs,
+    // so the merge's reads are spread over all contributing SMs instead of one.
+    // Arrivals happen above, before any wait, so every wait ends once the
+    // contributors' MMAs are done.
+    for (int pi = 0; pi < npend && !s_bail; ++pi) {
+      const int nt = pend[pi];
+      const int first_u = nt * a.kblocks, last_u = first_u + a.kblocks - 1;
+      const int c_first = owner(first_u, U, G), c_last = owner(last_u, U, G);
+      const int ncon = c_last - c_first + 1, me = (int)blockIdx.x - c_first;
+      if (etid == 0) {
+        uint32_t n = 0;
+        while (ld_acquire_gpu(&a.done[nt]) < ncon) {
+          if (++n >= kSpinLimit) { record_error(kDevTimeoutMerge); break; }
+          __nanosleep(64);
+        }
+      }
+      named_bar_sync(1, 128);
+      DBK_MARK(etid == 0 && pi == 0, 14);
+      const int total = a.batch * (kBN / 16);                    // items (batch row, 16 cols)
+      const int i0 = (int)((int64_t)me * total / ncon), i1 = (int)((int64_t)(me + 1) * total / ncon);
+      const int col0 = nt * kBN;
+      // This CTA's items are contiguous in every contributor's partial, so one bulk
+      // copy per (contributor, accumulator) brings them into the idle ring: all
+      // copies are in flight at once. Rounds bound the ring bytes used.
+      const size_t ring = (size_t)a.nstages * a.stage_bytes;
+      const int per_item = 64 * NACC * (ncon + 1);               // copies + sums
+      const int R = max(1, min(i1 - i0, (int)(ring / per_item)));
+      for (int ib = i0; ib < i1; ib += R) {
+        const int ni = min(R, i1 - ib);
+        const uint32_t piece = (uint32_t)ni * 64;                // bytes per copy
+        float* cp = reinterpret_cast<float*>(smem);              // [ncon][NACC][ni][16]
+        float* sm = cp + (size_t)ncon * NACC * ni * 16;          // [ni][NACC][16]
+        if (etid < 32) {
+          if (etid == 0) mbar_arrive_expect_tx(mrg_bar, piece * (uint32_t)(ncon * NACC));
+          __syncwarp();
+          asm volatile("fence.proxy.async.global;" ::: "memory");   // peers' generic stores
+          const uint64_t pol = policy_evict_first();
+          for (int w = etid; w < ncon * NACC; w += 32) {
+            const int c = c_first + w / NACC, acc = w % NACC;
+            const int sl = 2 * c + (range_start(c, U, G) >= first_u ? 0 : 1);
+            bulk_g2s(cp + (size_t)w * ni * 16,
+                     a.part + ((size_t)sl * NACC + acc) * a.batch * kBN + (size_t)ib * 16,
+                     piece, mrg_bar, pol);
+          }
+        }
+        if (!mbar_wait(mrg_bar, mphase, kDevTimeoutMerge)) { s_bail = 1; break; }
+        mphase ^= 1;
+        // sums in contributor order (deterministic)
+        for (int w = etid; w < ni * NACC * 16; w += 128) {
+          const int it = w / (NACC * 16), acc = (w / 16) % NACC, f = w & 15;
+          float t = 0.f;
+          for (int c = 0; c < ncon; ++c) t += cp[((size_t)(c * NACC + acc) * ni + it) * 16 + f];
+          sm[(it * NACC + acc) * 16 + f] = t;
+        }
+        named_bar_sync(1, 128);
+        DBK_MARK(etid == 0 && pi == 0 && ib == i0, 15);
+        for (int it = etid; it < ni; it += 128) {
+          const int item = ib + it, b = item / (kBN / 16), gq = item - b * (kBN / 16);
+          float g0[16], g1[16];
+#pragma unroll
+          for (int f = 0; f < 16; ++f) {
+            g0[f] = sm[(it * NACC + 0) * 16 + f];
+            g1[f] = (NACC == 2) ? sm[(it * NACC + (NACC - 1)) * 16 + f] : 0.f;
+          }
+          finish_row(col0, b, gq, g0, g1);
+        }
+        named_bar_sync(1, 128);                   // the ring is rewritten by the next round
+      }
+      // Departure: the last contributor to leave resets both counters for the next
+      // launch (which touches them only after its griddepcontrol.wait).
+      if (etid == 0) {
+        __threadfence();
+        if (atomicAdd(&a.done[a.ntiles + nt], 1) == ncon - 1) {
+          a.done[nt] = 0;
+          a.done[a.ntiles + nt] = 0;
+        }
+      }
     }
   }
   DBK_MARK(tid == 64, 7);
@@ -444,8 +538,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   // finished, and the TMEM release then stalled.)
   __syncwarp();
   tc_fence_before();
-  DBK_MARK(tid == 0, 14);
-  DBK_MARK(tid == 160, 15);
   if (lane == 0) mbar_arrive(teardown);
   if (warp == 1) {
     mbar_wait(teardown, 0, kDevTimeoutDrain);
@@ -481,14 +573,14 @@ TcPlan make_plan(int mode, bool split, int batch, int d_in, int d_out, int num_s
   static const int env_st = [] { const char* v = std::getenv("DBK_TC_STAGES"); return v ? std::atoi(v) : 12; }();
   const size_t fixed = 1024 + 512;
   p.nstages = env_st < 2 ? 2 : (env_st > 12 ? 12 : env_st);
-  while (p.nstages > 2 && fixed + (size_t)p.nstages * p.stage_bytes > (size_t)smem_optin - 4096)
+  while (p.nstages > 2 && fixed + (size_t)p.nstages * p.stage_bytes > (size_t)smem_optin - 6144)
     --p.nstages;
   p.smem = fixed + (size_t)p.nstages * p.stage_bytes;
   p.tmem_cols = (uint32_t)(nacc * kBN);
   p.ws_b = split ? (size_t)2 * p.nb * d_in * 2 : 0;
   p.ws_rms = (size_t)p.nb * sizeof(float);
   p.ws_part = (size_t)2 * num_sms * nacc * batch * kBN * sizeof(float);
-  p.ws_done = (size_t)p.ntiles * sizeof(int);
+  p.ws_done = (size_t)2 * p.ntiles * sizeof(int);
   p.ws_total = ((p.ws_b + 255) & ~(size_t)255) + ((p.ws_rms + 255) & ~(size_t)255) +
                ((p.ws_part + 255) & ~(size_t)255) + ((p.ws_done + 255) & ~(size_t)255);
   return p;
