@@ -124,6 +124,27 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // 32 lanes x 16 columns of fp32 from TMEM (this warp's lane quarter).
+// Two 16-column loads (e.g. gate and up accumulators) with one wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float (&va)[16],
+                                            float (&vb)[16]) {
+  uint32_t r[16], q[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(ta));
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]), "=r"(q[6]),
+        "=r"(q[7]), "=r"(q[8]), "=r"(q[9]), "=r"(q[10]), "=r"(q[11]), "=r"(q[12]), "=r"(q[13]),
+        "=r"(q[14]), "=r"(q[15])
+      : "r"(tb));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) { va[i] = __uint_as_float(r[i]); vb[i] = __uint_as_float(q[i]); }
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
   asm volatile(
@@ -328,6 +349,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     auto gather = [&](int acc, int gq, float (&v)[16]) {
       tmem_ld16(trow + acc * kBN + gq * 16, v);
       if constexpr (SPLIT) {
+        if (a.nb <= 16) {
+          // hi row r and lo row r + nb are lanes of the same warp (TMEM lanes 0..31)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] += __shfl_down_sync(0xffffffffu, v[i], a.nb);
+          return;
+        }
         if (r >= a.nb && r < a.nb + a.batch)
 #pragma unroll
           for (int i = 0; i < 16; ++i) xbuf[r - a.nb][i] = v[i];
@@ -336,6 +363,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] += xbuf[r][i];
         named_bar_sync(1, 128);
+      }
+    };
+    // Both accumulators of columns gq*16 .. +15 (one TMEM wait), hi + lo summed.
+    auto gather2 = [&](int gq, float (&v0)[16], float (&v1)[16]) {
+      if (SPLIT && a.nb > 16) {
+        gather(0, gq, v0);
+        gather(1, gq, v1);
+        return;
+      }
+      tmem_ld16x2(trow + gq * 16, trow + kBN + gq * 16, v0, v1);
+      if constexpr (SPLIT) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          v0[i] += __shfl_down_sync(0xffffffffu, v0[i], a.nb);
+          v1[i] += __shfl_down_sync(0xffffffffu, v1[i], a.nb);
+        }
       }
     };
     // Epilogue of batch row b, weight rows col0 + gq*16 .. +15.
@@ -373,8 +416,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       if (whole) {
         for (int gq = 0; gq < kBN / 16; ++gq) {
           float g0[16], g1[16];
-          gather(0, gq, g0);
-          if constexpr (NACC == 2) gather(1, gq, g1);
+          if constexpr (NACC == 2) gather2(gq, g0, g1);
+          else gather(0, gq, g0);
           finish(gq, g0, g1);
         }
         tc_fence_before();
@@ -387,15 +430,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       // Partial tile: publish this CTA's fp32 partial; the last contributor merges.
       const int slot = 2 * blockIdx.x + (u == u0 ? 0 : 1);
       for (int gq = 0; gq < kBN / 16; ++gq) {
+        float gv[NACC][16];
+        if constexpr (NACC == 2) gather2(gq, gv[0], gv[1]);
+        else gather(0, gq, gv[0]);
+        if (owner_row) {
 #pragma unroll
-        for (int acc = 0; acc < NACC; ++acc) {
-          float g0[16];
-          gather(acc, gq, g0);
-          if (owner_row) {
+          for (int acc = 0; acc < NACC; ++acc) {
             float* dst = a.part + (((size_t)slot * NACC + acc) * a.batch + r) * kBN + gq * 16;
 #pragma unroll
             for (int i = 0; i < 16; i += 4)
-              *reinterpret_cast<float4*>(dst + i) = make_float4(g0[i], g0[i + 1], g0[i + 2], g0[i + 3]);
+              *reinterpret_cast<float4*>(dst + i) =
+                  make_float4(gv[acc][i], gv[acc][i + 1], gv[acc][i + 2], gv[acc][i + 3]);
           }
         }
       }
