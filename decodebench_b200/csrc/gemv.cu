@@ -5,6 +5,8 @@
 //   MODE_NORM     y = inv_rms * W (x * gamma)                 (F1: RMSNorm -> GEMV)
 //   MODE_SWIGLU   h = silu(Wg x') * (Wu x'), x' = x or the    (F2: gate+up -> SwiGLU)
 //                 RMSNorm of x when gamma is given
+//   MODE_QKV      qkv = Wqkv x' with RoPE on q and k; q to     (QKV + RoPE + paged-KV append;
+//                 q_out, k and v into the paged cache          tensor-core variant only)
 //
 // Design (B200): the op is a pure HBM stream of W (2 bytes per weight, 1..8 FMAs
 // per weight), so the kernel is built to keep ~190 KB of weight bytes in flight
@@ -38,7 +40,20 @@
 namespace dbk {
 namespace {
 
-enum GemvMode : int { MODE_PLAIN = 0, MODE_NORM = 1, MODE_SWIGLU = 2 };
+enum GemvMode : int { MODE_PLAIN = 0, MODE_NORM = 1, MODE_SWIGLU = 2, MODE_QKV = 3 };
+
+// MODE_QKV operands (rows of Wqkv: the q heads, then the k heads, then the v
+// heads, head_dim rows each; inside a q or k head, row 2i holds dim i and row
+// 2i + 1 holds dim i + head_dim/2, so a RoPE pair is two adjacent rows).
+struct QkvArgs {
+  const int* pos;          // [batch] position of the new token (= cache slot)
+  const float* inv_freq;   // [head_dim / 2] rotary frequencies
+  void* q_out;             // [batch, hq, head_dim]
+  void* k_cache;           // [pages, hkv, page_size, head_dim] (or [batch, hkv, max_len, head_dim])
+  void* v_cache;
+  const int* page_table;   // [batch, max_pages] or nullptr (contiguous cache)
+  int hq, hkv, head_dim, page_size, max_pages;
+};
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
@@ -64,6 +79,7 @@ struct GemvArgs {
   long long y_ld;        // row stride of y and residual (elements)
   long long y_col0;      // column of y (and residual) where this op's rows start
   PeerSet ps;            // ps.world > 1: all-gather the output over the peers (fused)
+  QkvArgs qkv;           // MODE_QKV
 };
 
 // Shared-memory carve-up (dynamic): ring | full[] | empty[] | acc | inv_rms
@@ -311,8 +327,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
-  const int row0 = (int)(((int64_t)blockIdx.x * a.d_out) / G);
-  const int row1 = (int)(((int64_t)(blockIdx.x + 1) * a.d_out) / G);
+  // MODE_QKV: CTA row ranges start on even rows, so a RoPE pair never straddles CTAs
+  const int row0 = MODE == MODE_QKV ? 2 * (int)(((int64_t)blockIdx.x * (a.d_out / 2)) / G)
+                                    : (int)(((int64_t)blockIdx.x * a.d_out) / G);
+  const int row1 = MODE == MODE_QKV ? 2 * (int)(((int64_t)(blockIdx.x + 1) * (a.d_out / 2)) / G)
+                                    : (int)(((int64_t)(blockIdx.x + 1) * a.d_out) / G);
   const int nrows = row1 - row0;
   const int nmt = (nrows + RPT - 1) / RPT;
   const int total = nmt * a.nchunks;
@@ -473,6 +492,57 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
   named_bar_sync(1, kConsumers);
   DBK_MARK(tid == 0, 3);
 
+  if constexpr (MODE == MODE_QKV) {
+    // pairs of adjacent rows: RoPE on q and k, then q out and k, v into the cache
+    const QkvArgs& Q = a.qkv;
+    const int D = Q.head_dim, np = nrows / 2;
+    for (int idx = tid; idx < np * a.batch; idx += kConsumers) {
+      const int b = idx / np, r = 2 * (idx - b * np);
+      float v2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int mt = (r + e) / RPT, slot = (r + e) - mt * RPT;
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float* pr = part + ((size_t)w * nmt_max * 16 + mt * 16 + slot) * pc;
+          t += packed ? pr[b] + pr[a.batch + b] : pr[b];
+        }
+        v2[e] = t * inv_rms[b];
+      }
+      const int grow = row0 + r, head = grow / D, j = grow - head * D;   // j even
+      const int pos = Q.pos[b];
+      if (head < Q.hq + Q.hkv) {
+        const int i = j >> 1;
+        float sn, cs;
+        sincosf((float)pos * Q.inv_freq[i], &sn, &cs);
+        const float x0 = v2[0], x1 = v2[1];      // dims i and i + D/2
+        v2[0] = x0 * cs - x1 * sn;
+        v2[1] = x1 * cs + x0 * sn;
+      }
+      if (head < Q.hq) {
+        T* qo = static_cast<T*>(Q.q_out) + ((size_t)b * Q.hq + head) * D;
+        qo[j >> 1] = Elem<T>::from_f(v2[0]);
+        qo[(j >> 1) + D / 2] = Elem<T>::from_f(v2[1]);
+        continue;
+      }
+      const bool is_k = head < Q.hq + Q.hkv;
+      const int hk = head - Q.hq - (is_k ? 0 : Q.hkv);
+      if (pos < 0 || pos >= Q.page_size * Q.max_pages) continue;   // no slot: nothing cached
+      const int base = Q.page_table ? Q.page_table[(size_t)b * Q.max_pages + pos / Q.page_size] : b;
+      const int off = Q.page_table ? pos % Q.page_size : pos;
+      T* c = static_cast<T*>(is_k ? Q.k_cache : Q.v_cache) +
+             (((size_t)base * Q.hkv + hk) * Q.page_size + off) * D;
+      if (is_k) {
+        c[j >> 1] = Elem<T>::from_f(v2[0]);
+        c[(j >> 1) + D / 2] = Elem<T>::from_f(v2[1]);
+      } else {                                    // v rows are in natural order
+        c[j] = Elem<T>::from_f(v2[0]);
+        c[j + 1] = Elem<T>::from_f(v2[1]);
+      }
+    }
+    return;
+  }
   T* y = static_cast<T*>(a.y);
   const T* res = static_cast<const T*>(a.residual);
   for (int idx = tid; idx < nrows * a.batch; idx += kConsumers) {
@@ -585,7 +655,8 @@ int launch_t(const GemvArgs& a0, cudaStream_t st, const DeviceInfo& dev) {
   GemvArgs a = a0;
   {
     const int grid = a.d_out < dev.num_sms ? a.d_out : dev.num_sms;
-    a.max_rows = (a.d_out + grid - 1) / grid;
+    a.max_rows = (MODE == MODE_QKV) ? 2 * ((a.d_out / 2 + grid - 1) / grid)
+                                    : (a.d_out + grid - 1) / grid;
     const int rpt = (MODE == MODE_SWIGLU) ? 8 : 16;
     // x * gamma needs its low part; with batch <= 4 it rides in spare B columns
     a.pcols = (a.gamma != nullptr && 2 * a.batch <= 8) ? 2 * a.batch : a.batch;
@@ -598,10 +669,14 @@ int launch_t(const GemvArgs& a0, cudaStream_t st, const DeviceInfo& dev) {
     }
   }
   if (a.ps.world > 1) return DBK_ESHAPE;   // the fused all-gather needs the tensor-core variant
-  if (a.batch <= 1) return launch_nb<T, 1, MODE>(a, st, dev);
-  if (a.batch <= 2) return launch_nb<T, 2, MODE>(a, st, dev);
-  if (a.batch <= 4) return launch_nb<T, 4, MODE>(a, st, dev);
-  return launch_nb<T, 8, MODE>(a, st, dev);
+  if constexpr (MODE == MODE_QKV) {
+    return DBK_ESHAPE;                      // no CUDA-core variant of the QKV epilogue
+  } else {
+    if (a.batch <= 1) return launch_nb<T, 1, MODE>(a, st, dev);
+    if (a.batch <= 2) return launch_nb<T, 2, MODE>(a, st, dev);
+    if (a.batch <= 4) return launch_nb<T, 4, MODE>(a, st, dev);
+    return launch_nb<T, 8, MODE>(a, st, dev);
+  }
 }
 
 int gemv_dispatch(int mode, GemvArgs a, int dtype, cudaStream_t st) {
@@ -613,12 +688,14 @@ int gemv_dispatch(int mode, GemvArgs a, int dtype, cudaStream_t st) {
     switch (mode) {
       case MODE_PLAIN: return launch_t<__half, MODE_PLAIN>(a, st, dev);
       case MODE_NORM: return launch_t<__half, MODE_NORM>(a, st, dev);
+      case MODE_QKV: return launch_t<__half, MODE_QKV>(a, st, dev);
       default: return launch_t<__half, MODE_SWIGLU>(a, st, dev);
     }
   }
   switch (mode) {
     case MODE_PLAIN: return launch_t<__nv_bfloat16, MODE_PLAIN>(a, st, dev);
     case MODE_NORM: return launch_t<__nv_bfloat16, MODE_NORM>(a, st, dev);
+    case MODE_QKV: return launch_t<__nv_bfloat16, MODE_QKV>(a, st, dev);
     default: return launch_t<__nv_bfloat16, MODE_SWIGLU>(a, st, dev);
   }
 }
@@ -744,4 +821,30 @@ extern "C" int dbk_gemv_allgather(dbk_comm* comm, const void* x, const void* W,
   a.x = x; a.w0 = W; a.residual = residual_full; a.y = y_full;
   a.batch = batch; a.d_in = d_in; a.d_out = d_local;
   return gemv_ag(MODE_PLAIN, comm, a, dtype, stream);
+}
+
+// ---------------------------------------------------------------------------
+// QKV projection + RoPE + KV-cache append (batch 1..8).
+extern "C" int dbk_qkv_rope_append(const void* x, const void* gamma, const void* Wqkv,
+                                   const int32_t* positions, const float* inv_freq, void* q_out,
+                                   void* k_cache, void* v_cache, const int32_t* page_table,
+                                   int batch, int d_in, int n_q_heads, int n_kv_heads,
+                                   int head_dim, int page_size, int max_pages_per_seq,
+                                   float eps, int dtype, void* stream) {
+  const int d_out = (n_q_heads + 2 * n_kv_heads) * head_dim;
+  int rc = check_common(x, Wqkv, q_out, batch, d_in, d_out > 0 ? d_out : 1, dtype);
+  if (rc) return rc;
+  if (!positions || !inv_freq || !k_cache || !v_cache) return DBK_ENULL;
+  if (gamma && !aligned16(gamma)) return DBK_EALIGN;
+  if (n_q_heads < 1 || n_kv_heads < 1 || head_dim < 2 || head_dim % 2 || page_size < 1 ||
+      max_pages_per_seq < 1 || batch > kSimtMaxBatch)
+    return DBK_ESHAPE;
+  GemvArgs a{};
+  a.x = x; a.gamma = gamma; a.w0 = Wqkv; a.y = q_out;
+  a.batch = batch; a.d_in = d_in; a.d_out = d_out; a.eps = eps;
+  a.qkv.pos = positions; a.qkv.inv_freq = inv_freq; a.qkv.q_out = q_out;
+  a.qkv.k_cache = k_cache; a.qkv.v_cache = v_cache; a.qkv.page_table = page_table;
+  a.qkv.hq = n_q_heads; a.qkv.hkv = n_kv_heads; a.qkv.head_dim = head_dim;
+  a.qkv.page_size = page_size; a.qkv.max_pages = page_table ? max_pages_per_seq : 1;
+  return gemv_dispatch(MODE_QKV, a, dtype, static_cast<cudaStream_t>(stream));
 }

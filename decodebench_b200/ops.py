@@ -296,6 +296,66 @@ def flashdecode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     return o
 
 
+def interleave_rope_rows(Wqkv: torch.Tensor, n_q_heads: int, n_kv_heads: int,
+                         head_dim: int = 128) -> torch.Tensor:
+    """Wqkv in the usual layout ([q heads | k heads | v heads] x head_dim rows, natural
+    dim order) -> the layout qkv_rope_append streams: inside each q and k head, row
+    2i = dim i and row 2i + 1 = dim i + head_dim/2 (v heads unchanged). Done once
+    when the weights are loaded."""
+    h = head_dim // 2
+    perm = torch.stack([torch.arange(h), torch.arange(h) + h], dim=1).reshape(-1)
+    idx = [perm + head * head_dim for head in range(n_q_heads + n_kv_heads)]
+    idx.append(torch.arange((n_q_heads + n_kv_heads) * head_dim,
+                            (n_q_heads + 2 * n_kv_heads) * head_dim))
+    return Wqkv[torch.cat(idx).to(Wqkv.device)].contiguous()
+
+
+def rope_inv_freq(head_dim: int = 128, theta: float = 10000.0, device=None) -> torch.Tensor:
+    """theta^(-2i/head_dim), i < head_dim/2, in fp32 (as Llama's rotary embedding)."""
+    return 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64,
+                                         device=device).float() / head_dim))
+
+
+def qkv_rope_append(x: torch.Tensor, Wqkv_il: torch.Tensor, positions: torch.Tensor,
+                    inv_freq: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    n_q_heads: int, n_kv_heads: int, page_table: torch.Tensor | None = None,
+                    gamma: torch.Tensor | None = None, eps: float = 1e-5,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """QKV projection + RoPE + KV-cache append for one decode token per sequence.
+
+    x [batch, d_in]; Wqkv_il from :func:`interleave_rope_rows`; positions int32
+    [batch] (the new token's index = its cache slot); inv_freq fp32 [head_dim/2].
+    Paged caches (``page_table`` int32 [batch, max_pages]): [pages, Hkv, page_size, D];
+    contiguous: [batch, Hkv, max_len, D]. k and v are written into the caches in
+    place; returns q [batch, Hq, D] (rotated). With ``gamma``, x is RMS-normalised
+    first."""
+    dev = _need_cuda(x, Wqkv_il, positions, inv_freq, k_cache, v_cache, page_table, gamma, out)
+    dt = _dtype_code(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    batch, d_in = x2.shape
+    D = k_cache.shape[-1]
+    if Wqkv_il.shape != ((n_q_heads + 2 * n_kv_heads) * D, d_in):
+        raise ValueError(f"Wqkv must be [{(n_q_heads + 2 * n_kv_heads) * D}, {d_in}]")
+    if positions.dtype != torch.int32 or positions.numel() != batch:
+        raise ValueError("positions must be int32 [batch]")
+    if inv_freq.dtype != torch.float32 or inv_freq.numel() != D // 2:
+        raise ValueError(f"inv_freq must be float32 [{D // 2}]")
+    if k_cache.shape != v_cache.shape or k_cache.dtype != x.dtype or k_cache.shape[1] != n_kv_heads:
+        raise ValueError("k_cache / v_cache must share x's dtype and be [*, Hkv, slots, D]")
+    if page_table is None:
+        ps, maxp = k_cache.shape[2], 1
+    else:
+        if page_table.dtype != torch.int32 or page_table.dim() != 2 or page_table.shape[0] != batch:
+            raise ValueError("page_table must be int32 [batch, max_pages]")
+        ps, maxp = k_cache.shape[2], page_table.shape[1]
+    q = out if out is not None else torch.empty(batch, n_q_heads, D, dtype=x.dtype, device=dev)
+    N.check("dbk_qkv_rope_append", N.load().dbk_qkv_rope_append(
+        x2.data_ptr(), _ptr(gamma), Wqkv_il.data_ptr(), positions.data_ptr(), inv_freq.data_ptr(),
+        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _ptr(page_table), batch, d_in,
+        n_q_heads, n_kv_heads, D, ps, maxp, float(eps), dt, _stream(dev)))
+    return q
+
+
 def stage(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
     """Copy a decode step's input in, or its result out, with a small kernel.
 

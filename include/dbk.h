@@ -145,6 +145,29 @@ int dbk_flashdecode_noalloc(const void* q, const void* k_cache, const void* v_ca
                             int page_size, int max_pages_per_seq, float scale, int dtype,
                             void* stream);
 
+/* QKV projection + RoPE + KV-cache append for one decode token (batch 1..8):
+ *   qkv = Wqkv x'  (x' = RMSNorm(x) * gamma when gamma != NULL, else x; eps)
+ *   q, k get rotary embedding at position positions[b] (rotate-half / NeoX
+ *   pairing: dims i and i + head_dim/2, angle positions[b] * inv_freq[i]);
+ *   q -> q_out [batch, n_q_heads, head_dim]; k and v are written into the cache
+ *   slot positions[b]: paged (page_table != NULL, int32 [batch, max_pages]):
+ *   k_cache/v_cache [pages, n_kv_heads, page_size, head_dim]; contiguous
+ *   (page_table == NULL): [batch, n_kv_heads, page_size (= max_len), head_dim].
+ *   A position outside the cache writes q only.
+ * Wqkv [(n_q_heads + 2 n_kv_heads) * head_dim, d_in]: the q heads, the k heads,
+ * then the v heads; inside each q and k head the rows are pair-interleaved
+ * (row 2i = dim i, row 2i + 1 = dim i + head_dim/2; decodebench_b200.ops
+ * .interleave_rope_rows builds it from the usual layout once); v rows in
+ * natural order. inv_freq: fp32 [head_dim/2] on the device (e.g. theta^(-2i/D)).
+ * fp32 arithmetic, one rounding per output. This is the step before
+ * dbk_flashdecode in a decode layer; the reference has no such stage (README.md:106
+ * lists multi-output stages such as a QKV split or RoPE as unsupported). */
+int dbk_qkv_rope_append(const void* x, const void* gamma, const void* Wqkv,
+                        const int32_t* positions, const float* inv_freq, void* q_out,
+                        void* k_cache, void* v_cache, const int32_t* page_table, int batch,
+                        int d_in, int n_q_heads, int n_kv_heads, int head_dim, int page_size,
+                        int max_pages_per_seq, float eps, int dtype, void* stream);
+
 /* ------------------------------------------------------------------------
  * Shard-boundary all-gather over NVLink peer memory (multi-GPU, one process
  * per GPU). No counterpart in the reference, which is single-GPU: it replaces
