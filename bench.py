@@ -650,7 +650,114 @@ class MLP(Workload):
         return 2 * (2 * self.cpu_rows * self.d)
 
 
-WORKLOADS = {"f2": F2, "f1": F1, "f4": F4, "gqa": GQA, "mlp": MLP}
+class QKV(Workload):
+    """The step before FlashDecode (next row of the scope, not a BASELINE config):
+    RMSNorm -> QKV projection -> RoPE -> KV-cache append, Llama-3-8B shapes:
+    x [1, 4096] fp16, Wqkv [(32 + 2 x 8) x 128, 4096], paged cache (64-token pages).
+    With N ranks each owns Hq/N query and Hkv/N kv heads (the attention that
+    follows is sharded the same way), so no exchange is needed."""
+
+    name = "qkv"
+    exchanges_per_step = 0
+
+    def __init__(self, rank, world, torch, d=4096, hq=32, hkv=8, D=128, ps=64):
+        import numpy as np
+
+        from decodebench_b200 import costs, ops
+
+        self.t, self.ops, self.costs = torch, ops, costs
+        self.rank, self.world, self.batch, self.d_in = rank, world, 1, d
+        if hkv % world:
+            raise SystemExit(f"{hkv} kv heads do not split over {world} ranks")
+        self.hq_total, self.hkv_total, self.D = hq, hkv, D
+        self.hq, self.hkv = hq // world, hkv // world
+        self.rows = (self.hq + 2 * self.hkv) * D
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(31 + rank)
+        per_rep = self.rows * d * 2
+        self.nrep = min(64, max(2, math.ceil(2 * 126e6 / per_rep)))
+        self.W = [ops.interleave_rope_rows(
+            (torch.randn(self.rows, d, generator=g, device=dev) / 64).half(), self.hq, self.hkv, D)
+            for _ in range(self.nrep)]
+        xg = torch.Generator().manual_seed(42)
+        self.x_cpu = torch.randn(1, d, generator=xg).half()
+        self.g_cpu = torch.randn(d, generator=xg).half()
+        self.x, self.gamma = self.x_cpu.to(dev), self.g_cpu.to(dev)
+        self.inv_freq = ops.rope_inv_freq(D, 500000.0, device=dev)
+        self.max_pages = 128
+        self.pos = torch.tensor([self.max_pages * ps - 1000], dtype=torch.int32, device=dev)
+        self.table = torch.from_numpy(np.arange(self.max_pages, dtype=np.int32)[None, :]).to(dev)
+        self.kc = torch.zeros(self.max_pages, self.hkv, ps, D, dtype=torch.float16, device=dev)
+        self.vc = torch.zeros_like(self.kc)
+        self.q = torch.empty(1, self.hq, D, dtype=torch.float16, device=dev)
+
+    def describe(self):
+        return {"workload": "QKV projection + RoPE + paged KV append (the step before FlashDecode), "
+                            f"x [1,{self.d_in}] fp16, Wqkv [{(self.hq_total + 2 * self.hkv_total) * self.D},"
+                            f"{self.d_in}] fp16, 32 q / 8 kv heads, head_dim 128",
+                "global_batch": 1, "d_in": self.d_in,
+                "parallelism": ("single GPU" if self.world == 1 else
+                                f"heads sharded ({self.hq} q / {self.hkv} kv per rank), no exchange"),
+                "weight_replicas": self.nrep,
+                "l2": f"weights rotated over {self.nrep} replicas "
+                      f"({self.nrep * self.rows * self.d_in * 2 / 1e6:.0f} MB per GPU > 126 MB L2)"}
+
+    def _bytes(self, rows, hq, hkv):
+        return rows * self.d_in * 2 + 2 * self.d_in * 2 + hq * self.D * 2 + 2 * hkv * self.D * 2
+
+    def step_bytes_total(self):
+        return self._bytes((self.hq_total + 2 * self.hkv_total) * self.D, self.hq_total, self.hkv_total)
+
+    def launch_bytes(self):
+        return self._bytes(self.rows, self.hq, self.hkv)
+
+    def run_kernel(self, rep):
+        self.ops.qkv_rope_append(self.x, self.W[rep % self.nrep], self.pos, self.inv_freq,
+                                 self.kc, self.vc, self.hq, self.hkv, page_table=self.table,
+                                 gamma=self.gamma, out=self.q)
+
+    def exchange(self):
+        pass
+
+    def e2e_setup(self):
+        t = self.t
+        self.x_host = self.x_cpu.pin_memory()
+        self.out_host = t.empty(self.q.numel(), dtype=t.float16).pin_memory()
+        self.x_dev = t.empty_like(self.x)
+        self._e2e_i = 0
+        return self.x_host.nbytes, self.out_host.nbytes
+
+    def e2e_step(self):
+        W = self.W[self._e2e_i % self.nrep]
+        self._e2e_i += 1
+        self.ops.stage(self.x_dev, self.x_host)
+        q = self.ops.qkv_rope_append(self.x_dev, W, self.pos, self.inv_freq, self.kc, self.vc,
+                                     self.hq, self.hkv, page_table=self.table, gamma=self.gamma,
+                                     out=self.q)
+        self.ops.stage(self.out_host, q.reshape(-1))
+
+    # CPU: the reference's gemv_ref over a sample of the weight rows (the projection
+    # is the whole cost of the step)
+    def cpu_setup(self, frac_rows: float = 1.0):
+        import numpy as np
+
+        rng = np.random.default_rng(5)
+        n = max(1, int(self.rows * frac_rows))
+        self.cpu_rows = n
+        self.cW = (rng.standard_normal((n, self.d_in), dtype=np.float32) / 64
+                   ).astype(np.float16).astype(np.float32)
+        self.cx = self.x_cpu.float().numpy()[0].copy()
+
+    def cpu_step(self, threads):
+        from oracle import oracle as O
+
+        return O.ref_gemv_threaded(self.cW, self.cx, threads)
+
+    def cpu_step_bytes(self):
+        return self.cpu_rows * self.d_in * 2
+
+
+WORKLOADS = {"f2": F2, "f1": F1, "f4": F4, "gqa": GQA, "mlp": MLP, "qkv": QKV}
 
 
 # ---------------------------------------------------------------- timing

@@ -36,7 +36,7 @@ def build_parser() -> argparse.ArgumentParser:
     sub = ap.add_subparsers(dest="command", required=True)
 
     d = sub.add_parser("demo", help="Run a bundled Llama-decode demo.")
-    d.add_argument("name", choices=["f1", "f2", "f4"], help="Demo name.")
+    d.add_argument("name", choices=["f1", "f2", "f4", "layer"], help="Demo name.")
     d.add_argument("--dim", type=int, choices=[2048, 4096], default=4096, help="Hidden dimension.")
     d.add_argument("--batch", type=int, default=1, help="Batch size.")
     d.add_argument("--trials", type=int, default=30, help="Number of timing trials.")
@@ -55,7 +55,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--dry-run", action="store_true", help="Print plan and exit.")
 
     s = sub.add_parser("sweep", help="Sweep batch sizes and hidden dims for a demo.")
-    s.add_argument("name", choices=["f1", "f2", "f4"], help="Demo name.")
+    s.add_argument("name", choices=["f1", "f2", "f4", "layer"], help="Demo name.")
     s.add_argument("--batch", type=parse_comma_list, default=[1, 2, 4, 8],
                    help="Comma-separated batch sizes to sweep.")
     s.add_argument("--dim", type=int, choices=[2048, 4096], default=4096, help="Hidden dimension.")
@@ -96,6 +96,12 @@ def _fused_bytes(name: str, inputs: dict) -> int:
     if name == "f2":
         b, d = inputs["xh"].shape
         return costs.gateup_swiglu_bytes(b, d, inputs["Wg"].shape[0])
+    if name == "layer":
+        # every weight once, the cached K/V of each sequence once, x in, y out
+        w = sum(inputs[k].nbytes for k in ("Wqkv_il", "Wo", "Wg", "Wu", "Wd"))
+        b, hkv, _, dh = inputs["Kc"].shape
+        kv = 2 * int(inputs["lens"].sum().item()) * hkv * dh * inputs["Kc"].element_size()
+        return w + kv + 2 * inputs["x"].nbytes
     b, h, L, dh = inputs["K"].shape
     return costs.flashdecode_bytes([L] * b, h, h, dh)
 

@@ -363,6 +363,22 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             fence_proxy_async_smem();   // order these writes before the next TMA refill
             __syncwarp();
           }
+          if (w.tt == w.ntb - 1 && n - 1 >= t0 && n - 1 < t0 + 16) {
+            // The newest token's K/V may come from the kernel just before this one
+            // (e.g. dbk_qkv_rope_append): the producer streamed this tile before
+            // that kernel had finished, so re-read that one row pair now, after
+            // griddepcontrol.wait. Lane l < 16: 16 bytes of K; l >= 16: of V.
+            const int tok = n - 1, cc = lane & 15;
+            int run;
+            const int64_t rr = kv_rowidx(a, w.b, w.hk, w.tt * kTile + tok, &run);
+            const T* src = static_cast<const T*>(lane < 16 ? a.k : a.v) + rr * kD + cc * 8;
+            const int line = (tok >> 4) * 32 + (cc >> 3) * 16 + (tok & 15);
+            uint8_t* dst = smem + (size_t)s * kStage + (lane < 16 ? 0 : kStage / 2) + line * 128 +
+                           (((cc & 7) ^ (line & 7)) << 4);
+            *reinterpret_cast<uint4*>(dst) = __ldcg(reinterpret_cast<const uint4*>(src));
+            fence_proxy_async_smem();
+            __syncwarp();
+          }
           // S^T[16 tokens x 8 heads] = K Q^T: tokens are the M rows (no padding);
           // heads 0..G-1 are the N columns. Two accumulators halve the MMA chain.
           float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
@@ -443,6 +459,18 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
     } else {
       if (!DBK_TIMED_WAIT(tid == 0, 11, mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull))) return;
       const int mine = min(8, n - warp * 8);           // tokens of this warp
+      if (w.tt == w.ntb - 1 && n - 1 >= warp * 8 && n - 1 < warp * 8 + 8) {
+        // newest token re-read after griddepcontrol.wait (see the tensor-core path)
+        const int tok = n - 1, cc = lane & 15;
+        int run;
+        const int64_t rr = kv_rowidx(a, w.b, w.hk, w.tt * kTile + tok, &run);
+        const T* src = static_cast<const T*>(lane < 16 ? a.k : a.v) + rr * kD + cc * 8;
+        uint8_t* dst = smem + (size_t)s * kStage + (lane < 16 ? 0 : kStage / 2) +
+                       (size_t)tok * kD * sizeof(T) + cc * 16;
+        *reinterpret_cast<uint4*>(dst) = __ldcg(reinterpret_cast<const uint4*>(src));
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
       if (mine > 0) {
         const uint32_t kbase = kst + (uint32_t)((warp * 8) * kD + 4 * lane) * sizeof(T);
         const uint32_t vbase = kbase + kStage / 2;

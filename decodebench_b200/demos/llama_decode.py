@@ -19,7 +19,7 @@ import math
 from ..sequence import Sequence
 from ..timing import n_weight_replicas
 
-DEMO_NAMES = ("f1", "f2", "f4")
+DEMO_NAMES = ("f1", "f2", "f4", "layer")
 _FFN = {2048: 8192, 4096: 11008}
 _L = 1024
 _HEAD_DIM = 128
@@ -127,7 +127,123 @@ def _build_f4(dim: int, batch: int, gen):
     return seq, inputs, _replicas(inputs, ("K", "V")), fused
 
 
-_BUILDERS = {"f1": _build_f1, "f2": _build_f2, "f4": _build_f4}
+def _build_layer(dim: int, batch: int, gen):
+    """One whole Llama decode layer for a single new token per sequence (the
+    reference's demos stop at single fused ops; README.md:7-14 frames the layer as
+    the unit whose launch overhead matters).
+
+    Unfused: the stage chain below in PyTorch (each stage one tensor; attention
+    rotates and attends to the new token's k/v next to the cached ones without
+    writing the cache). Fused: five sm_100a kernels chained with programmatic
+    dependent launch: QKV + RoPE + cache append, FlashDecode over the cache,
+    o_proj + residual, RMSNorm + gate/up + SwiGLU, down + residual."""
+    import torch
+
+    from .. import ops
+
+    ff = _FFN[dim]
+    H, Hkv, D, L = dim // _HEAD_DIM, max(1, dim // _HEAD_DIM // 4), _HEAD_DIM, _L
+    sc = 1.0 / math.sqrt(dim)
+    x = _randn(gen, batch, dim)
+    g1 = _randn(gen, dim, scale=0.5)
+    g2 = _randn(gen, dim, scale=0.5)
+    Wqkv = _randn(gen, (H + 2 * Hkv) * D, dim, scale=sc)
+    Wo = _randn(gen, dim, H * D, scale=1.0 / math.sqrt(H * D))
+    Wg = _randn(gen, ff, dim, scale=sc)
+    Wu = _randn(gen, ff, dim, scale=sc)
+    Wd = _randn(gen, dim, ff, scale=1.0 / math.sqrt(ff))
+    cap = L + 64                                   # cache slots; the new token goes to slot L
+    Kc = _randn(gen, batch, Hkv, cap, D)
+    Vc = _randn(gen, batch, Hkv, cap, D)
+    pos = torch.full((batch,), L, dtype=torch.int32, device="cuda")
+    lens = torch.full((batch,), L + 1, dtype=torch.int32, device="cuda")
+    inv_freq = ops.rope_inv_freq(D, 500000.0, device="cuda")
+    ang = pos.float()[:, None] * inv_freq[None, :]
+    cos, sin = torch.cos(ang), torch.sin(ang)      # [batch, D/2] fp32
+    Wqkv_il = ops.interleave_rope_rows(Wqkv, H, Hkv, D)
+    seq = Sequence("layer")
+
+    def _rms(t, g):
+        var = t.float().pow(2).mean(dim=-1, keepdim=True)
+        return (t.float() * torch.rsqrt(var + 1e-5)).half() * g
+
+    def _rot(t, c, s):                             # t [B, heads, D]
+        t1, t2 = t[..., :D // 2].float(), t[..., D // 2:].float()
+        c, s = c[:, None, :], s[:, None, :]
+        return torch.cat([t1 * c - t2 * s, t2 * c + t1 * s], dim=-1).half()
+
+    @seq.stage
+    def attn_norm(x, g1):
+        return _rms(x, g1)
+
+    @seq.stage
+    def qkv(attn_norm, Wqkv):
+        return torch.nn.functional.linear(attn_norm, Wqkv)
+
+    @seq.stage
+    def q_rot(qkv, cos, sin):
+        return _rot(qkv[:, :H * D].reshape(-1, H, D), cos, sin).contiguous()
+
+    @seq.stage
+    def attn(q_rot, qkv, Kc, Vc, cos, sin):
+        B = q_rot.shape[0]
+        k_new = _rot(qkv[:, H * D:(H + Hkv) * D].reshape(B, Hkv, D), cos, sin)
+        v_new = qkv[:, (H + Hkv) * D:].reshape(B, Hkv, D)
+        K = torch.cat([Kc[:, :, :L], k_new[:, :, None]], dim=2)       # [B, Hkv, L+1, D]
+        V = torch.cat([Vc[:, :, :L], v_new[:, :, None]], dim=2)
+        K = K.repeat_interleave(H // Hkv, dim=1)
+        V = V.repeat_interleave(H // Hkv, dim=1)
+        s = torch.einsum("bhd,bhld->bhl", q_rot.float(), K.float()) / math.sqrt(D)
+        p = torch.softmax(s, dim=-1)
+        return torch.einsum("bhl,bhld->bhd", p, V.float()).half().reshape(B, H * D)
+
+    @seq.stage
+    def o_proj(attn, Wo):
+        return torch.nn.functional.linear(attn, Wo)
+
+    @seq.stage
+    def resid1(o_proj, x):
+        return o_proj + x
+
+    @seq.stage
+    def mlp_norm(resid1, g2):
+        return _rms(resid1, g2)
+
+    @seq.stage
+    def gate(mlp_norm, Wg):
+        return torch.nn.functional.linear(mlp_norm, Wg)
+
+    @seq.stage
+    def up(mlp_norm, Wu):
+        return torch.nn.functional.linear(mlp_norm, Wu)
+
+    @seq.stage
+    def swiglu(up, gate):
+        return torch.nn.functional.silu(gate) * up
+
+    @seq.stage
+    def down(swiglu, Wd):
+        return torch.nn.functional.linear(swiglu, Wd)
+
+    @seq.stage
+    def resid2(down, resid1):
+        return down + resid1
+
+    def fused(inp):
+        q = ops.qkv_rope_append(inp["x"], inp["Wqkv_il"], inp["pos"], inp["inv_freq"],
+                                inp["Kc"], inp["Vc"], H, Hkv, gamma=inp["g1"], eps=1e-5)
+        o = ops.flashdecode(q, inp["Kc"], inp["Vc"], seq_lens=inp["lens"])
+        h = ops.gemv(o.reshape(o.shape[0], -1), inp["Wo"], residual=inp["x"])
+        a = ops.gateup_swiglu(h, inp["Wg"], inp["Wu"], gamma=inp["g2"], eps=1e-5)
+        return ops.gemv(a, inp["Wd"], residual=h)
+
+    inputs = {"x": x, "g1": g1, "g2": g2, "Wqkv": Wqkv, "Wqkv_il": Wqkv_il, "Wo": Wo, "Wg": Wg,
+              "Wu": Wu, "Wd": Wd, "Kc": Kc, "Vc": Vc, "cos": cos, "sin": sin, "pos": pos,
+              "lens": lens, "inv_freq": inv_freq}
+    return seq, inputs, _replicas(inputs, ("Wqkv", "Wqkv_il", "Wo", "Wg", "Wu", "Wd")), fused
+
+
+_BUILDERS = {"f1": _build_f1, "f2": _build_f2, "f4": _build_f4, "layer": _build_layer}
 
 
 def build_demo(name: str, dim: int = 4096, batch: int = 1, seed: int = 42):

@@ -115,13 +115,15 @@ int dbk_gemv(const void* x, const void* W, const void* residual, void* y,
  * Replaces f4_partial_kernel + f4_reduce_kernel (validation/src/kernels/fused/f4.cu:173-319,
  * launched at bench_variant.cu:758-763) and the Python stages scores, softmax,
  * weighted_v (llama_decode.py:120-134). head_dim 128 only.
- * Ordering (programmatic dependent launch): q is read, and out and the
- * workspace are written, only after every earlier kernel in the stream has
- * completed; seq_lens, the page table and the K/V cache are read earlier, while
- * the preceding kernel may still run. This matters only when the preceding
- * kernel is one of this library's (other kernels never release their
- * dependents early): do not have the immediately preceding dbk_* call write
- * them, or put an event / any other kernel between, or set DBK_PDL=0. */
+ * Ordering (programmatic dependent launch): q, and each sequence's newest K/V
+ * row (the one a preceding dbk_qkv_rope_append writes), are read, and out and
+ * the workspace written, only after every earlier kernel in the stream has
+ * completed. seq_lens, the page table and the rest of the cache
+ * are read earlier, while the preceding kernel may still run. That matters
+ * only when the preceding kernel is one of this library's (other kernels never
+ * release their dependents early): such a call may write the newest token's
+ * K/V but not older slots, seq_lens or the page table; otherwise put an event
+ * or any other kernel between, or set DBK_PDL=0. */
 int dbk_flashdecode(const void* q, const void* k_cache, const void* v_cache,
                     const int32_t* page_table, const int32_t* seq_lens, void* out,
                     int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len,
