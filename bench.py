@@ -757,7 +757,87 @@ class QKV(Workload):
         return self.cpu_rows * self.d_in * 2
 
 
-WORKLOADS = {"f2": F2, "f1": F1, "f4": F4, "gqa": GQA, "mlp": MLP, "qkv": QKV}
+class Layer(Workload):
+    """One whole Llama decode layer for one new token (the scope's next rows, not a
+    BASELINE config): d 4096, 32 q / 8 kv heads, FFN 11008, fp16, contiguous cache
+    of 1024 tokens + the new one; five kernels chained with programmatic dependent
+    launch (QKV + RoPE + append, FlashDecode, o_proj + residual, RMSNorm + gate/up
+    + SwiGLU, down + residual). Single GPU: a sharded layer needs a reduction after
+    o_proj and down, which this build does not provide."""
+
+    name = "layer"
+    kernels_per_step = 5
+    exchanges_per_step = 0
+
+    def __init__(self, rank, world, torch):
+        if world > 1:
+            raise SystemExit("the layer workload runs on one GPU")
+        from decodebench_b200.demos.llama_decode import build_demo
+
+        self.t = torch
+        self.rank, self.world, self.batch = rank, world, 1
+        _, self.inputs, self.reps, self.fused = build_demo("layer", dim=4096, batch=1)
+        self.nrep = len(self.reps)
+        self.out = None
+
+    def describe(self):
+        return {"workload": "whole Llama decode layer, d 4096, 32 q / 8 kv heads, FFN 11008, fp16, "
+                            "1024 cached tokens + 1 new", "global_batch": 1,
+                "parallelism": "single GPU", "weight_replicas": self.nrep,
+                "l2": f"weights rotated over {self.nrep} replicas (> 126 MB L2 each)"}
+
+    def step_bytes_total(self):
+        inp = self.inputs
+        w = sum(inp[k].nbytes for k in ("Wqkv_il", "Wo", "Wg", "Wu", "Wd"))
+        _, hkv, _, dh = inp["Kc"].shape
+        kv = 2 * (1024 + 1) * hkv * dh * 2
+        return w + kv + 2 * inp["x"].nbytes
+
+    def launch_bytes(self):
+        return self.step_bytes_total()
+
+    def run_kernel(self, rep):
+        self.out = self.fused(self.reps[rep % self.nrep])
+
+    def exchange(self):
+        pass
+
+    def e2e_setup(self):
+        t = self.t
+        self.x_host = self.inputs["x"].cpu().pin_memory()
+        self.out_host = t.empty(self.inputs["x"].numel(), dtype=t.float16).pin_memory()
+        self._e2e_i = 0
+        return self.x_host.nbytes, self.out_host.nbytes
+
+    def e2e_step(self):
+        from decodebench_b200 import ops
+
+        r = self.reps[self._e2e_i % self.nrep]
+        self._e2e_i += 1
+        ops.stage(r["x"], self.x_host)
+        y = self.fused(r)
+        ops.stage(self.out_host, y.reshape(-1))
+
+    def cpu_setup(self, frac_rows: float = 1.0):
+        import numpy as np
+
+        rng = np.random.default_rng(5)
+        rows = 6144 + 4096 + 2 * 11008
+        n = max(1, int(rows * frac_rows))
+        self.cpu_rows = n
+        self.cW = (rng.standard_normal((n, 4096), dtype=np.float32) / 64).astype(np.float16).astype(np.float32)
+        self.cx = self.inputs["x"].float().cpu().numpy()[0].copy()
+
+    def cpu_step(self, threads):
+        from oracle import oracle as O
+
+        return O.ref_gemv_threaded(self.cW, self.cx, threads)
+
+    def cpu_step_bytes(self):
+        return self.cpu_rows * 4096 * 2
+
+
+WORKLOADS = {"f2": F2, "f1": F1, "f4": F4, "gqa": GQA, "mlp": MLP, "qkv": QKV, "layer": Layer}
 
 
 # ---------------------------------------------------------------- timing

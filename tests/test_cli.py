@@ -38,3 +38,12 @@ def test_gpu_commands_fail_cleanly_without_gpu(capsys):
         pytest.skip("has a GPU")
     assert main(["demo", "f1"]) == 1
     assert "GPU/CUDA is not available" in capsys.readouterr().err
+
+
+def test_layer_demo_is_a_choice(capsys):
+    from decodebench_b200.cli import main
+    from decodebench_b200.demos.llama_decode import DEMO_NAMES
+
+    assert "layer" in DEMO_NAMES
+    assert main(["demo", "layer", "--dry-run"]) == 0
+    assert "layer" in capsys.readouterr().out
