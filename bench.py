@@ -650,6 +650,69 @@ class MLP(Workload):
         return 2 * (2 * self.cpu_rows * self.d)
 
 
+class F2FP8(F2):
+    """F2 (config C2's shape) with e4m3 weights and per-row fp32 scales: the weight
+    stream is half of C2's bytes (scope's next rows: low-precision weight formats;
+    not a BASELINE config). Single GPU."""
+
+    name = "f2fp8"
+
+    def __init__(self, rank, world, torch, d_in=4096, d_ff=11008, batch=1):
+        if world > 1:
+            raise SystemExit("the f2fp8 workload runs on one GPU")
+        from decodebench_b200 import costs, ops
+
+        self.t, self.ops, self.costs = torch, ops, costs
+        self.rank, self.world = rank, world
+        self.d_in, self.d_ff, self.batch, self.rows = d_in, d_ff, batch, d_ff
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(1234)
+        sc = 1.0 / math.sqrt(d_in)
+        per_rep = 2 * d_ff * d_in
+        self.nrep = min(64, max(2, math.ceil(2 * 126e6 / per_rep)))
+        self.W = []
+        for _ in range(self.nrep):
+            Wg8, sg = ops.quantize_fp8_rows(torch.randn(d_ff, d_in, generator=g, device=dev) * sc)
+            Wu8, su = ops.quantize_fp8_rows(torch.randn(d_ff, d_in, generator=g, device=dev) * sc)
+            self.W.append((Wg8, sg, Wu8, su))
+        xg = torch.Generator().manual_seed(42)
+        self.x_cpu = torch.randn(batch, d_in, generator=xg).half()
+        self.x = self.x_cpu.to(dev)
+        self.h_local = torch.empty(batch, d_ff, dtype=torch.float16, device=dev)
+        self.h_full = self.h_local
+
+    def describe(self):
+        return {"workload": f"F2 gate+up GEMV -> SwiGLU with e4m3 weights + per-row fp32 scales, "
+                            f"x [{self.batch},{self.d_in}] fp16, Wg/Wu [{self.d_ff},{self.d_in}] fp8",
+                "global_batch": self.batch, "d_in": self.d_in, "d_ff": self.d_ff,
+                "parallelism": "single GPU", "weight_replicas": self.nrep,
+                "l2": f"weights rotated over {self.nrep} replicas "
+                      f"({self.nrep * 2 * self.d_ff * self.d_in / 1e6:.0f} MB > 126 MB L2)"}
+
+    def _bytes(self):
+        return 2 * self.d_ff * self.d_in + 2 * self.d_ff * 4 + self.batch * (self.d_in + self.d_ff) * 2
+
+    def step_bytes_total(self):
+        return self._bytes()
+
+    def launch_bytes(self):
+        return self._bytes()
+
+    def run_kernel(self, rep):
+        Wg8, sg, Wu8, su = self.W[rep % self.nrep]
+        self.ops.gateup_swiglu_fp8(self.x, Wg8, sg, Wu8, su, out=self.h_local)
+
+    def exchange(self):
+        pass
+
+    def e2e_step(self):
+        Wg8, sg, Wu8, su = self.W[self._e2e_i % self.nrep]
+        self._e2e_i += 1
+        self.ops.stage(self.x_dev, self.x_host)
+        h = self.ops.gateup_swiglu_fp8(self.x_dev, Wg8, sg, Wu8, su, out=self.h_local)
+        self.ops.stage(self.out_host, h.reshape(-1))
+
+
 class QKV(Workload):
     """The step before FlashDecode (next row of the scope, not a BASELINE config):
     RMSNorm -> QKV projection -> RoPE -> KV-cache append, Llama-3-8B shapes:
@@ -837,7 +900,8 @@ class Layer(Workload):
         return self.cpu_rows * 4096 * 2
 
 
-WORKLOADS = {"f2": F2, "f1": F1, "f4": F4, "gqa": GQA, "mlp": MLP, "qkv": QKV, "layer": Layer}
+WORKLOADS = {"f2": F2, "f1": F1, "f4": F4, "gqa": GQA, "mlp": MLP, "qkv": QKV, "layer": Layer,
+             "f2fp8": F2FP8}
 
 
 # ---------------------------------------------------------------- timing

@@ -45,6 +45,9 @@ SIGNATURES = {
     "dbk_gateup_swiglu_allgather": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P]),
     "dbk_gemv_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "dbk_copy": (_I, [_P, _P, _SZ, _P]),
+    "dbk_gemv_fp8": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "dbk_rmsnorm_gemv_fp8": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P]),
+    "dbk_gateup_swiglu_fp8": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P]),
     "dbk_qkv_rope_append": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I,
                                  _F, _I, _P]),
 }

@@ -32,6 +32,7 @@
 // (src/decodebench/demos/llama_decode.py:36-43, :77-87): fp32 accumulation,
 // silu(g) = g / (1 + exp(-g)) (f2.cu:73), output rounded once to fp16/bf16.
 #include <cstdlib>
+#include <type_traits>
 
 #include "comm.cuh"
 #include "common.cuh"
@@ -80,6 +81,8 @@ struct GemvArgs {
   long long y_col0;      // column of y (and residual) where this op's rows start
   PeerSet ps;            // ps.world > 1: all-gather the output over the peers (fused)
   QkvArgs qkv;           // MODE_QKV
+  const float* wscale0;  // fp8 weights: per-row scale of w0 (and of w1); nullptr for 16-bit W
+  const float* wscale1;
 };
 
 // Shared-memory carve-up (dynamic): ring | full[] | empty[] | acc | inv_rms
@@ -304,13 +307,35 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(const GemvArgs
 //   * SwiGLU: an m-tile holds 8 gate rows (rows 0..7) and the 8 up rows of the
 //     same outputs (rows 8..15), so the epilogue reads gate and up of an output
 //     from neighbouring partial rows.
+// Two e4m3 bytes (the low or the high half of a 32-bit register) -> f16x2; every
+// e4m3 value is exact in fp16.
+__device__ __forceinline__ uint32_t e4m3x2_lo(uint32_t r) {
+  uint32_t d;
+  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; cvt.rn.f16x2.e4m3x2 %0, l; }" : "=r"(d) : "r"(r));
+  return d;
+}
+__device__ __forceinline__ uint32_t e4m3x2_hi(uint32_t r) {
+  uint32_t d;
+  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; cvt.rn.f16x2.e4m3x2 %0, h; }" : "=r"(d) : "r"(r));
+  return d;
+}
+
 constexpr int kMmaKC = 2048;
+constexpr int kMmaKC8 = 4096;                 // fp8 weights: same 4 KB row segments
 constexpr int kMmaSlot = kMmaKC * 2 + 16;     // padded row slot (bytes)
 constexpr int kMmaStage = 16 * kMmaSlot;      // 65,792 bytes
 constexpr int kMmaStages = 3;
 
-template <typename T, int MODE, bool SPLIT>
+// W8: weights are e4m3 bytes with a per-row fp32 scale. A stage then holds 4096
+// columns; ldmatrix on the bytes gives each lane 4 consecutive k of a row, which
+// are widened to f16 and used as the mma's k slots (2q, 2q+1, 2q+8, 2q+9) -- the
+// activation fragment is loaded with the same k order, so the dot product is
+// unchanged. The activation is staged in fp16 (hi + lo) whatever T is.
+template <typename T, int MODE, bool SPLIT, bool W8 = false>
 __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a) {
+  using MT = typename std::conditional<W8, __half, T>::type;   // mma / staging type
+  constexpr int KC = W8 ? kMmaKC8 : kMmaKC;
+  constexpr int WB = W8 ? 1 : (int)sizeof(T);                 // bytes per weight
   constexpr int NMAT = (MODE == MODE_SWIGLU) ? 2 : 1;
   constexpr int RPT = 16 / NMAT;                  // output rows per m-tile
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -351,25 +376,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      const T* W0 = static_cast<const T*>(a.w0);
-      const T* W1 = static_cast<const T*>(a.w1);
+      const uint8_t* W0 = static_cast<const uint8_t*>(a.w0);
+      const uint8_t* W1 = static_cast<const uint8_t*>(a.w1);
       for (int j = 0; j < total; ++j) {
         const int s = j % a.nstages;
         if (j >= a.nstages &&
             !DBK_TIMED_WAIT(true, 10, mbar_wait(&empty[s], ((j / a.nstages) & 1) ^ 1, kDevTimeoutEmpty)))
           return;
         const int mt = j / a.nchunks, c = j - mt * a.nchunks;
-        const int col0 = c * kMmaKC;
-        const int seg = min(kMmaKC, a.d_in - col0);
+        const int col0 = c * KC;
+        const int seg = min(KC, a.d_in - col0);
         const int r_first = row0 + mt * RPT;
         const int valid = min(RPT, row1 - r_first);
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(valid * NMAT * seg * sizeof(T)));
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(valid * NMAT * seg * WB));
         uint8_t* dst = ring + (size_t)s * kMmaStage;
         for (int q = 0; q < valid; ++q) {
-          const size_t off = (size_t)(r_first + q) * a.d_in + col0;
-          bulk_g2s(dst + q * kMmaSlot, W0 + off, (uint32_t)(seg * sizeof(T)), &full[s], pol);
+          const size_t off = ((size_t)(r_first + q) * a.d_in + col0) * WB;
+          bulk_g2s(dst + q * kMmaSlot, W0 + off, (uint32_t)(seg * WB), &full[s], pol);
           if constexpr (NMAT == 2)
-            bulk_g2s(dst + (8 + q) * kMmaSlot, W1 + off, (uint32_t)(seg * sizeof(T)), &full[s], pol);
+            bulk_g2s(dst + (8 + q) * kMmaSlot, W1 + off, (uint32_t)(seg * WB), &full[s], pol);
         }
       }
     }
@@ -402,9 +427,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
         float p0 = f[e], p1 = f[e + 1];
         sq = fmaf(p0, p0, fmaf(p1, p1, sq));
         if (gam != nullptr) { p0 *= g[e]; p1 *= g[e + 1]; }
-        hi[e / 2] = Mma<T>::pack(p0, p1);
-        const float2 h = Elem<T>::unpack2(hi[e / 2]);
-        lo[e / 2] = Mma<T>::pack(p0 - h.x, p1 - h.y);
+        hi[e / 2] = Mma<MT>::pack(p0, p1);
+        const float2 h = Elem<MT>::unpack2(hi[e / 2]);
+        lo[e / 2] = Mma<MT>::pack(p0 - h.x, p1 - h.y);
       }
 #pragma unroll
       for (int bb = 0; bb < 8; ++bb) ss[bb] += (bb == b) ? sq : 0.f;
@@ -436,20 +461,50 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
   const int bn = lane >> 2;                  // B column held by this lane
   const bool packed = SPLIT && pc > a.batch;  // columns [batch, 2 batch) hold the low parts
   const bool b_ok = bn < pc;
+  const int kq = (W8 ? 4 : 2) * (lane & 3);   // this lane's first k in a 16- (32-) k step
   const uint16_t* xh =
       (packed && bn >= a.batch ? xs_lo + (size_t)(bn - a.batch) * a.d_in
-                               : xs_hi + (size_t)(b_ok ? bn : 0) * a.d_in) + 2 * (lane & 3);
-  const uint16_t* xl = xs_lo + (size_t)(b_ok && bn < a.batch ? bn : 0) * a.d_in + 2 * (lane & 3);
+                               : xs_hi + (size_t)(b_ok ? bn : 0) * a.d_in) + kq;
+  const uint16_t* xl = xs_lo + (size_t)(b_ok && bn < a.batch ? bn : 0) * a.d_in + kq;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
 
   for (int j = 0; j < total; ++j) {
     const int s = j % a.nstages;
     const int mt = j / a.nchunks, c = j - mt * a.nchunks;
-    const int col0 = c * kMmaKC;
-    const int seg = min(kMmaKC, a.d_in - col0);
+    const int col0 = c * KC;
+    const int seg = min(KC, a.d_in - col0);
     if (!DBK_TIMED_WAIT(tid == 0, 11, mbar_wait(&full[s], (j / a.nstages) & 1, kDevTimeoutFull))) return;
     DBK_MARK(tid == 0 && j == 0, 2);
     const uint32_t stage = smem_u32(ring + (size_t)s * kMmaStage) + a_lane_off;
+    if constexpr (W8) {
+#pragma unroll 4
+      for (int kk = 0; kk < 16; ++kk) {
+        const int k = warp * 512 + kk * 32;     // 32 fp8 columns = 32 bytes per row
+        if (k < seg) {
+          uint32_t af[4];
+          ldsm_x4(stage + k, af);               // rows g / g+8, bytes k+4q..+3 and k+16+4q..+3
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t ra = af[2 * h], rb = af[2 * h + 1];
+            const int kx = col0 + k + 16 * h;
+            uint32_t b0 = 0u, b1 = 0u;
+            if (b_ok) {
+              b0 = *reinterpret_cast<const uint32_t*>(xh + kx);
+              b1 = *reinterpret_cast<const uint32_t*>(xh + kx + 2);
+            }
+            Mma<__half>::run(acc, e4m3x2_lo(ra), e4m3x2_lo(rb), e4m3x2_hi(ra), e4m3x2_hi(rb), b0, b1);
+            if (SPLIT && !packed) {
+              uint32_t l0 = 0u, l1 = 0u;
+              if (b_ok) {
+                l0 = *reinterpret_cast<const uint32_t*>(xl + kx);
+                l1 = *reinterpret_cast<const uint32_t*>(xl + kx + 2);
+              }
+              Mma<__half>::run(acc, e4m3x2_lo(ra), e4m3x2_lo(rb), e4m3x2_hi(ra), e4m3x2_hi(rb), l0, l1);
+            }
+          }
+        }
+      }
+    } else
 #pragma unroll 4
     for (int kk = 0; kk < 16; ++kk) {
       const int k = warp * 256 + kk * 16;
@@ -558,13 +613,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
       return t;
     };
     float v;
+    const float s0 = W8 ? a.wscale0[row0 + r] : 1.f;
     if constexpr (MODE == MODE_SWIGLU) {
       const float sc = inv_rms[b];
-      v = silu(sum_row(q) * sc) * (sum_row(8 + q) * sc);
+      const float s1 = W8 ? a.wscale1[row0 + r] : 1.f;
+      v = silu(sum_row(q) * sc * s0) * (sum_row(8 + q) * sc * s1);
     } else if constexpr (MODE == MODE_NORM) {
-      v = sum_row(q) * inv_rms[b];
+      v = sum_row(q) * inv_rms[b] * s0;
     } else {
-      v = sum_row(q);
+      v = sum_row(q) * s0;
     }
     const size_t o = (size_t)b * a.y_ld + a.y_col0 + row0 + r;
     if (res != nullptr) v += Elem<T>::to_f(res[o]);
@@ -612,11 +669,22 @@ size_t mma_smem_bytes(const GemvArgs& a, int rpt, int nst) {
 
 template <typename T, int MODE>
 int launch_mma(GemvArgs a, cudaStream_t st, const DeviceInfo& dev, size_t smem) {
-  a.kc = kMmaKC;
-  a.nchunks = (a.d_in + kMmaKC - 1) / kMmaKC;
-  const void* kern = (a.gamma != nullptr)   // x alone is exact in 16 bits: no low part
-                         ? reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, true>)
-                         : reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, false>);
+  const bool w8 = a.wscale0 != nullptr;
+  a.kc = w8 ? kMmaKC8 : kMmaKC;
+  a.nchunks = (a.d_in + a.kc - 1) / a.kc;
+  // x alone is exact in 16 bits: no low part (except for fp8 weights with bf16 x,
+  // whose activation is restaged in fp16)
+  const bool split = a.gamma != nullptr || (w8 && std::is_same<T, __nv_bfloat16>::value);
+  const void* kern;
+  if constexpr (MODE == MODE_QKV) {
+    kern = split ? reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, true>)
+                 : reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, false>);
+  } else {
+    kern = w8 ? (split ? reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, true, true>)
+                       : reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, false, true>))
+              : (split ? reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, true>)
+                       : reinterpret_cast<const void*>(gemv_mma_kernel<T, MODE, false>));
+  }
   if (int rc = allow_dynamic_smem(reinterpret_cast<const void*>(kern), dev, smem)) return rc;
   return launch_pdl(kern, dim3(a.d_out < dev.num_sms ? a.d_out : dev.num_sms), dim3(kThreads),
                     smem, st, &a);
@@ -659,7 +727,9 @@ int launch_t(const GemvArgs& a0, cudaStream_t st, const DeviceInfo& dev) {
                                     : (a.d_out + grid - 1) / grid;
     const int rpt = (MODE == MODE_SWIGLU) ? 8 : 16;
     // x * gamma needs its low part; with batch <= 4 it rides in spare B columns
-    a.pcols = (a.gamma != nullptr && 2 * a.batch <= 8) ? 2 * a.batch : a.batch;
+    const bool split = a.gamma != nullptr ||
+                       (a.wscale0 != nullptr && std::is_same<T, __nv_bfloat16>::value);
+    a.pcols = (split && 2 * a.batch <= 8) ? 2 * a.batch : a.batch;
     for (int nst = kMmaStages; nst >= 2 && !simt_only; --nst) {
       const size_t smem = mma_smem_bytes(a, rpt, nst);
       if (smem != 0 && smem <= (size_t)dev.max_smem_optin - 1024) {
@@ -668,7 +738,8 @@ int launch_t(const GemvArgs& a0, cudaStream_t st, const DeviceInfo& dev) {
       }
     }
   }
-  if (a.ps.world > 1) return DBK_ESHAPE;   // the fused all-gather needs the tensor-core variant
+  if (a.ps.world > 1 || a.wscale0 != nullptr)
+    return DBK_ESHAPE;   // the fused all-gather and fp8 weights need the tensor-core variant
   if constexpr (MODE == MODE_QKV) {
     return DBK_ESHAPE;                      // no CUDA-core variant of the QKV epilogue
   } else {
@@ -847,4 +918,52 @@ extern "C" int dbk_qkv_rope_append(const void* x, const void* gamma, const void*
   a.qkv.hq = n_q_heads; a.qkv.hkv = n_kv_heads; a.qkv.head_dim = head_dim;
   a.qkv.page_size = page_size; a.qkv.max_pages = page_table ? max_pages_per_seq : 1;
   return gemv_dispatch(MODE_QKV, a, dtype, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------
+// fp8 (e4m3) weights with a per-row fp32 scale, batch 1..8: half the weight bytes
+// of the 16-bit entry points. y[b, r] = scale[r] * sum_k W8[r, k] x'[b, k].
+namespace {
+int check_fp8(const void* x, const void* w, const float* sc, const void* y, int batch, int d_in,
+              int d_out, int dtype) {
+  if (int rc = check_common(x, w, y, batch, d_in, d_out, dtype)) return rc;
+  if (!sc) return DBK_ENULL;
+  if (batch > kSimtMaxBatch || d_in % 32 != 0) return DBK_ESHAPE;
+  return DBK_OK;
+}
+}  // namespace
+
+extern "C" int dbk_gemv_fp8(const void* x, const void* W8, const float* w_scale,
+                            const void* residual, void* y, int batch, int d_in, int d_out,
+                            int dtype, void* stream) {
+  if (int rc = check_fp8(x, W8, w_scale, y, batch, d_in, d_out, dtype)) return rc;
+  GemvArgs a{};
+  a.x = x; a.w0 = W8; a.wscale0 = w_scale; a.residual = residual; a.y = y;
+  a.batch = batch; a.d_in = d_in; a.d_out = d_out;
+  return gemv_dispatch(MODE_PLAIN, a, dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dbk_rmsnorm_gemv_fp8(const void* x, const void* gamma, const void* W8,
+                                    const float* w_scale, void* y, int batch, int d_in,
+                                    int d_out, float eps, int dtype, void* stream) {
+  if (int rc = check_fp8(x, W8, w_scale, y, batch, d_in, d_out, dtype)) return rc;
+  if (!gamma) return DBK_ENULL;
+  if (!aligned16(gamma)) return DBK_EALIGN;
+  GemvArgs a{};
+  a.x = x; a.gamma = gamma; a.w0 = W8; a.wscale0 = w_scale; a.y = y;
+  a.batch = batch; a.d_in = d_in; a.d_out = d_out; a.eps = eps;
+  return gemv_dispatch(MODE_NORM, a, dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dbk_gateup_swiglu_fp8(const void* x, const void* gamma, const void* Wg8,
+                                     const float* g_scale, const void* Wu8,
+                                     const float* u_scale, void* h, int batch, int d_in,
+                                     int d_ff, float eps, int dtype, void* stream) {
+  if (int rc = check_fp8(x, Wg8, g_scale, h, batch, d_in, d_ff, dtype)) return rc;
+  if (!Wu8 || !u_scale) return DBK_ENULL;
+  if (!aligned16(Wu8) || (gamma && !aligned16(gamma))) return DBK_EALIGN;
+  GemvArgs a{};
+  a.x = x; a.gamma = gamma; a.w0 = Wg8; a.w1 = Wu8; a.wscale0 = g_scale; a.wscale1 = u_scale;
+  a.y = h; a.batch = batch; a.d_in = d_in; a.d_out = d_ff; a.eps = eps;
+  return gemv_dispatch(MODE_SWIGLU, a, dtype, static_cast<cudaStream_t>(stream));
 }

@@ -356,6 +356,68 @@ def qkv_rope_append(x: torch.Tensor, Wqkv_il: torch.Tensor, positions: torch.Ten
     return q
 
 
+def quantize_fp8_rows(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row e4m3 quantisation for the fp8 GEMVs: returns (W8, scale) with
+    W ~= scale[:, None] * W8.float(); scale = amax(|row|) / 448 (fp32)."""
+    Wf = W.float()
+    scale = (Wf.abs().amax(dim=1) / 448.0).clamp_min(1e-30)
+    W8 = (Wf / scale[:, None]).to(torch.float8_e4m3fn).contiguous()
+    return W8, scale.contiguous()
+
+
+def gemv_fp8(x: torch.Tensor, W8: torch.Tensor, w_scale: torch.Tensor,
+             residual: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``linear(x, scale * W8) (+ residual)``, e4m3 weights with per-row scales, batch <= 8."""
+    dev = _need_cuda(x, W8, w_scale, residual, out)
+    x2, d_out = x.reshape(-1, x.shape[-1]), W8.shape[0]
+    _check_fp8(x2, W8, w_scale)
+    y = out if out is not None else torch.empty(*x.shape[:-1], d_out, dtype=x.dtype, device=dev)
+    N.check("dbk_gemv_fp8", N.load().dbk_gemv_fp8(
+        x2.data_ptr(), W8.data_ptr(), w_scale.data_ptr(), _ptr(residual), y.data_ptr(),
+        x2.shape[0], x2.shape[1], d_out, _dtype_code(x), _stream(dev)))
+    return y
+
+
+def rmsnorm_gemv_fp8(x: torch.Tensor, gamma: torch.Tensor, W8: torch.Tensor,
+                     w_scale: torch.Tensor, eps: float = 1e-6,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """F1 with e4m3 weights: ``linear(rmsnorm(x) * gamma, scale * W8)``."""
+    dev = _need_cuda(x, gamma, W8, w_scale, out)
+    x2, d_out = x.reshape(-1, x.shape[-1]), W8.shape[0]
+    _check_fp8(x2, W8, w_scale)
+    y = out if out is not None else torch.empty(*x.shape[:-1], d_out, dtype=x.dtype, device=dev)
+    N.check("dbk_rmsnorm_gemv_fp8", N.load().dbk_rmsnorm_gemv_fp8(
+        x2.data_ptr(), gamma.data_ptr(), W8.data_ptr(), w_scale.data_ptr(), y.data_ptr(),
+        x2.shape[0], x2.shape[1], d_out, float(eps), _dtype_code(x), _stream(dev)))
+    return y
+
+
+def gateup_swiglu_fp8(x: torch.Tensor, Wg8: torch.Tensor, g_scale: torch.Tensor,
+                      Wu8: torch.Tensor, u_scale: torch.Tensor,
+                      gamma: torch.Tensor | None = None, eps: float = 1e-6,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """F2 with e4m3 weights: ``silu(x (sg Wg8)^T) * (x (su Wu8)^T)``, optional RMSNorm."""
+    dev = _need_cuda(x, Wg8, g_scale, Wu8, u_scale, gamma, out)
+    x2, d_ff = x.reshape(-1, x.shape[-1]), Wg8.shape[0]
+    _check_fp8(x2, Wg8, g_scale)
+    _check_fp8(x2, Wu8, u_scale)
+    h = out if out is not None else torch.empty(*x.shape[:-1], d_ff, dtype=x.dtype, device=dev)
+    N.check("dbk_gateup_swiglu_fp8", N.load().dbk_gateup_swiglu_fp8(
+        x2.data_ptr(), _ptr(gamma), Wg8.data_ptr(), g_scale.data_ptr(), Wu8.data_ptr(),
+        u_scale.data_ptr(), h.data_ptr(), x2.shape[0], x2.shape[1], d_ff, float(eps),
+        _dtype_code(x), _stream(dev)))
+    return h
+
+
+def _check_fp8(x2, W8, scale):
+    if W8.dtype != torch.float8_e4m3fn:
+        raise TypeError(f"fp8 weights must be torch.float8_e4m3fn, got {W8.dtype}")
+    if scale.dtype != torch.float32 or scale.numel() != W8.shape[0]:
+        raise ValueError("scale must be float32 with one value per weight row")
+    if W8.dim() != 2 or W8.shape[1] != x2.shape[1]:
+        raise ValueError(f"shape mismatch: x {tuple(x2.shape)}, W8 {tuple(W8.shape)}")
+
+
 def stage(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
     """Copy a decode step's input in, or its result out, with a small kernel.
 

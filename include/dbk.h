@@ -170,6 +170,24 @@ int dbk_qkv_rope_append(const void* x, const void* gamma, const void* Wqkv,
                         int d_in, int n_q_heads, int n_kv_heads, int head_dim, int page_size,
                         int max_pages_per_seq, float eps, int dtype, void* stream);
 
+/* fp8 weights (batch 1..8): W8 holds e4m3 bytes (OCP FP8, torch.float8_e4m3fn),
+ * row-major [d_out, d_in], with one fp32 scale per row: the weight is
+ * scale[r] * W8[r, k]. Same operations and argument rules as dbk_gemv,
+ * dbk_rmsnorm_gemv and dbk_gateup_swiglu, with d_in % 32 == 0, x and y fp16 or
+ * bf16 (dtype), fp32 accumulation; the activation is used in fp16 (hi + lo
+ * parts), so |x * gamma| must stay below 65504. The activation is staged in
+ * shared memory: batch * d_in up to about 22,000 (DBK_ESHAPE beyond). Half the weight bytes of the
+ * 16-bit entry points, for an HBM-bound decode step. No counterpart in the
+ * reference (README.md:118 lists quantization as out of its scope). */
+int dbk_gemv_fp8(const void* x, const void* W8, const float* w_scale, const void* residual,
+                 void* y, int batch, int d_in, int d_out, int dtype, void* stream);
+int dbk_rmsnorm_gemv_fp8(const void* x, const void* gamma, const void* W8, const float* w_scale,
+                         void* y, int batch, int d_in, int d_out, float eps, int dtype,
+                         void* stream);
+int dbk_gateup_swiglu_fp8(const void* x, const void* gamma, const void* Wg8, const float* g_scale,
+                          const void* Wu8, const float* u_scale, void* h, int batch, int d_in,
+                          int d_ff, float eps, int dtype, void* stream);
+
 /* ------------------------------------------------------------------------
  * Shard-boundary all-gather over NVLink peer memory (multi-GPU, one process
  * per GPU). No counterpart in the reference, which is single-GPU: it replaces
