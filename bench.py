@@ -2,13 +2,20 @@
 """Benchmark of the fused decode hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload f2|f1|f4|gqa|mlp]
+                    [--workload f2|f1|f4|gqa|mlp|qkv|layer|f2fp8]
+
+The benchmark's five configs: C1 F1 RMSNorm -> GEMV 4096x4096 fp16; C2 F2
+gate+up -> SwiGLU, Wg/Wu [11008,4096] fp16; C3 F4 MHA FlashDecode, 32 heads x
+4096 tokens; C4 Llama-70B decode MLP, batch 16, bf16; C5 GQA paged FlashDecode,
+batch 8, 64/8 heads, lengths ~U[1024,32768]. qkv, layer and f2fp8 are the
+added rows (QKV + RoPE + cache append, a whole decode layer, fp8 weights).
 
 A step is one pass of the fused hot path over one decode batch. The default
-workload is BASELINE config 2 (F2: gate+up GEMV -> SwiGLU, x [1,4096] fp16,
+workload is config C2 (F2: gate+up GEMV -> SwiGLU, x [1,4096] fp16,
 Wg/Wu [11008,4096] fp16 ~N(0,1)/64). With N GPUs (torchrun, one process per
-GPU, NCCL) the weights are column-sharded (d_ff/N rows per rank) and the step
-ends with an NCCL all-gather of h: total work is fixed ("strong" scaling).
+GPU) the weights are column-sharded (d_ff/N rows per rank) and the all-gather
+of h runs inside the GEMV kernel over NVLink peer memory (NCCL with
+DBK_EXCHANGE=nccl): total work is fixed ("strong" scaling).
 
 Reported:
   value      whole-job HBM GB/s = algorithmic bytes of a step / max-over-ranks
@@ -171,7 +178,7 @@ class Workload:
 
 
 class F2(Workload):
-    """x [1,4096] fp16, Wg/Wu [11008,4096] fp16 ~N(0,1)/64."""
+    """config C2: x [1,4096] fp16, Wg/Wu [11008,4096] fp16 ~N(0,1)/64."""
 
     name = "f2"
 
@@ -201,7 +208,7 @@ class F2(Workload):
 
     def describe(self):
         return {"workload": f"F2 gate+up GEMV -> SwiGLU, x [{self.batch},{self.d_in}] fp16, "
-                            f"Wg/Wu [{self.d_ff},{self.d_in}] fp16 (BASELINE config 2)",
+                            f"Wg/Wu [{self.d_ff},{self.d_in}] fp16 (config C2)",
                 "global_batch": self.batch, "d_in": self.d_in, "d_ff": self.d_ff,
                 "parallelism": ("single GPU" if self.world == 1 else
                                 f"tp{self.world}: d_ff column-sharded, {self.xname()} of h"),
@@ -281,7 +288,7 @@ class F2(Workload):
 
 
 class F1(F2):
-    """BASELINE config 1 on the GPU: RMSNorm -> GEMV, 4096 x 4096 fp16."""
+    """config C1 on the GPU: RMSNorm -> GEMV, 4096 x 4096 fp16."""
 
     name = "f1"
 
@@ -359,7 +366,7 @@ class F1(F2):
 
 
 class F4(Workload):
-    """q [1,32,1,128]; K,V [1,32,4096,128] fp16, scale 1/sqrt(128).
+    """config C3: q [1,32,1,128]; K,V [1,32,4096,128] fp16, scale 1/sqrt(128).
     With N ranks the heads are sharded (32/N per rank), out all-gathered."""
 
     name = "f4"
@@ -385,7 +392,7 @@ class F4(Workload):
 
     def describe(self):
         return {"workload": f"F4 split-KV FlashDecode MHA, q [{self.batch},{self.H},1,128], "
-                            f"K/V [{self.batch},{self.H},{self.L},128] fp16 (BASELINE config 3)",
+                            f"K/V [{self.batch},{self.H},{self.L},128] fp16 (config C3)",
                 "global_batch": self.batch, "heads": self.H, "kv_len": self.L,
                 "parallelism": ("single GPU" if self.world == 1 else
                                 f"heads sharded {self.h}/rank, {self.xname()} of out"),
@@ -443,7 +450,7 @@ class F4(Workload):
 
 
 class GQA(F4):
-    """batch 8, 64 q heads, 8 kv heads, head_dim 128, bf16 paged
+    """config C5: batch 8, 64 q heads, 8 kv heads, head_dim 128, bf16 paged
     KV (64-token pages, random page permutation), lengths ~U[1024, 32768] seeded.
     With N ranks the kv heads are sharded (8/N per rank with their 8 q heads)."""
 
@@ -489,7 +496,7 @@ class GQA(F4):
 
     def describe(self):
         return {"workload": "GQA paged FlashDecode, batch 8, 64 q / 8 kv heads, head_dim 128, "
-                            "bf16, 64-token pages, lengths ~U[1024,32768] (BASELINE config 5)",
+                            "bf16, 64-token pages, lengths ~U[1024,32768] (config C5)",
                 "global_batch": self.batch, "seq_lens": [int(x) for x in self.lens_np],
                 "parallelism": ("single GPU" if self.world == 1 else
                                 f"kv heads sharded {self.hkv}/rank, {self.xname()} of out"),
@@ -549,7 +556,7 @@ class GQA(F4):
 
 
 class MLP(Workload):
-    """Llama-70B-shaped decode MLP, batch 16, d 8192, d_ff 28672,
+    """config C4: Llama-70B-shaped decode MLP, batch 16, d 8192, d_ff 28672,
     bf16; RMSNorm (eps 1e-5) -> gate/up -> SwiGLU -> down. With N ranks gate/up
     and down are column-sharded; h is all-gathered between them and y at the end."""
 
@@ -580,7 +587,7 @@ class MLP(Workload):
 
     def describe(self):
         return {"workload": "Llama-70B-shaped decode MLP, batch 16, d 8192, d_ff 28672, bf16: "
-                            "RMSNorm -> gate/up -> SwiGLU -> down (BASELINE config 4)",
+                            "RMSNorm -> gate/up -> SwiGLU -> down (config C4)",
                 "global_batch": self.batch, "d_model": self.d, "d_ff": self.d_ff,
                 "parallelism": ("single GPU" if self.world == 1 else
                                 f"tp{self.world}: gate/up and down column-sharded, "
@@ -653,7 +660,7 @@ class MLP(Workload):
 class F2FP8(F2):
     """F2 (config C2's shape) with e4m3 weights and per-row fp32 scales: the weight
     stream is half of C2's bytes (scope's next rows: low-precision weight formats;
-    not a BASELINE config). Single GPU."""
+    not one of the five benchmark configs). Single GPU."""
 
     name = "f2fp8"
 
@@ -714,7 +721,7 @@ class F2FP8(F2):
 
 
 class QKV(Workload):
-    """The step before FlashDecode (next row of the scope, not a BASELINE config):
+    """The step before FlashDecode (next row of the scope, not one of the five benchmark configs):
     RMSNorm -> QKV projection -> RoPE -> KV-cache append, Llama-3-8B shapes:
     x [1, 4096] fp16, Wqkv [(32 + 2 x 8) x 128, 4096], paged cache (64-token pages).
     With N ranks each owns Hq/N query and Hkv/N kv heads (the attention that
@@ -822,7 +829,7 @@ class QKV(Workload):
 
 class Layer(Workload):
     """One whole Llama decode layer for one new token (the scope's next rows, not a
-    BASELINE config): d 4096, 32 q / 8 kv heads, FFN 11008, fp16, contiguous cache
+    benchmark config): d 4096, 32 q / 8 kv heads, FFN 11008, fp16, contiguous cache
     of 1024 tokens + the new one; five kernels chained with programmatic dependent
     launch (QKV + RoPE + append, FlashDecode, o_proj + residual, RMSNorm + gate/up
     + SwiGLU, down + residual). Single GPU: a sharded layer needs a reduction after
@@ -1183,7 +1190,7 @@ def _cpu_only_init(wl, name, torch):
         wl.d_ff = 11008 if name == "f2" else 4096
         wl.x_cpu = torch.randn(1, wl.d_in, generator=gen).half()
         wl.g_cpu = torch.randn(wl.d_in, generator=gen).half()
-        label = ("F2 gate+up GEMV -> SwiGLU, x [1,4096] fp16, Wg/Wu [11008,4096] (BASELINE config 2)"
+        label = ("F2 gate+up GEMV -> SwiGLU, x [1,4096] fp16, Wg/Wu [11008,4096] (config C2)"
                  if name == "f2" else "F1 RMSNorm -> GEMV, x [1,4096], W [4096,4096]")
         wl.describe_cpu = lambda: {"workload": label, "global_batch": 1, "d_in": 4096,
                                    "d_ff": wl.d_ff, "parallelism": "CPU host threads"}

@@ -6,7 +6,7 @@
 //   PLAIN  y = W x (+ residual)          NORM  y = inv_rms * W (x * gamma)
 //   SWIGLU h = silu(Wg x') * (Wu x')      (x' = x, or RMSNorm(x) when gamma is given)
 //
-// At batch 16 the Llama-70B MLP does 16 flop per weight byte:
+// At batch 16 the Llama-70B MLP (config C4) does 16 flop per weight byte:
 // still HBM-bound, but too much work for CUDA cores (~300 us of fp32 FMA vs
 // ~210 us of HBM time), so the contraction runs on the 5th-generation tensor
 // cores while the kernel stays a weight stream:

@@ -5,7 +5,7 @@ The unfused chains keep the reference's stage code semantics
 roundings) -> gemv; F2 gate, up, swiglu; F4 scores (no scale), softmax, weighted_v.
 Unlike the reference, inputs are drawn from a seeded CPU generator (the
 reference allocates before its seed call, sequence.py:228) and use
-BASELINE-style scaling so fp16 stays far from overflow: W ~ N(0,1)/sqrt(d) and,
+benchmark-style scaling so fp16 stays far from overflow: W ~ N(0,1)/sqrt(d) and,
 for F4, q ~ N(0, 1/128) so the unscaled scores have unit variance.
 
 ``build_demo`` returns (seq, inputs, replicas, fused) where ``fused`` is the

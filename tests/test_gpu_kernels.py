@@ -1,6 +1,6 @@
 """GPU parity of the sm_100a kernels (through the C ABI via decodebench_b200.ops)
 against the CPU oracle, the reference's golden stage outputs, and
-size-independent properties at the BASELINE sizes."""
+size-independent properties at the benchmark sizes."""
 
 from __future__ import annotations
 

@@ -1,5 +1,5 @@
 """GPU parity of the batch > 8 tensor-core (tcgen05) path: oracle at small and
-ragged shapes, and the full Llama-70B-shaped decode MLP
+ragged shapes, and the full Llama-70B-shaped decode MLP (config C4)
 against a torch fp32 reference computed on the GPU from the same bf16 inputs
 (the C oracle would take minutes at that size)."""
 
@@ -74,7 +74,7 @@ def test_tc_deterministic_stream_k(ops):
 
 
 def test_mlp_c4_full_size(ops):
-    """batch 16, d 8192, d_ff 28672, bf16, eps 1e-5."""
+    """config C4: batch 16, d 8192, d_ff 28672, bf16, eps 1e-5."""
     torch.manual_seed(0)
     dev = "cuda"
     B, D, F = 16, 8192, 28672
