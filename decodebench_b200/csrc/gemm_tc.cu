@@ -563,7 +563,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
           }
           finish_row(col0, b, gq, g0, g1);
         }
-        named_bar_sync(1, 128);                   // the ring is rewritten by the next round
+        named_bar_sync(1, 128);                   // the ring is rewritten by the next batch of items
       }
       // Departure: the last contributor to leave resets both counters for the next
       // launch (which touches them only after its griddepcontrol.wait).
