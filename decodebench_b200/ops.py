@@ -46,6 +46,21 @@ def _need_cuda(*ts: torch.Tensor) -> torch.device:
     return dev
 
 
+def _check_out(out: torch.Tensor | None, dev: torch.device) -> None:
+    """``out`` may be a CUDA tensor on ``dev`` or a pinned CPU tensor: the kernel then
+    writes the result straight into host memory (through its unified address), which
+    saves the separate copy-out of a decode step. Any other CPU tensor is refused."""
+    if out is None:
+        return
+    if not out.is_contiguous():
+        raise ValueError("out must be contiguous")
+    if out.is_cuda:
+        if out.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    elif not out.is_pinned():
+        raise RuntimeError("out must be a CUDA tensor or a pinned CPU tensor (no CPU fallback)")
+
+
 def _ptr(t):
     return None if t is None else t.data_ptr()
 
@@ -138,7 +153,8 @@ def rmsnorm_gemv(x: torch.Tensor, gamma: torch.Tensor, W: torch.Tensor, eps: flo
                             y.data_ptr(), x2.shape[0], x2.shape[1], W.shape[0], float(eps),
                             _dtype_code(x), _stream(x.device)),
                         lambda: rmsnorm_gemv(x2, gamma, W, eps=eps, workspace=workspace))
-    dev = _need_cuda(x, gamma, W, out)
+    dev = _need_cuda(x, gamma, W)
+    _check_out(out, dev)
     dt = _dtype_code(x)
     if gamma.dtype != x.dtype or W.dtype != x.dtype:
         raise TypeError("x, gamma and W must share one dtype")
@@ -177,7 +193,8 @@ def gateup_swiglu(x: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
                             float(eps), _dtype_code(x), _stream(x.device)),
                         lambda: gateup_swiglu(x2, Wg, Wu, gamma=gamma, eps=eps,
                                               workspace=workspace))
-    dev = _need_cuda(x, Wg, Wu, gamma, out)
+    dev = _need_cuda(x, Wg, Wu, gamma)
+    _check_out(out, dev)
     dt = _dtype_code(x)
     x2 = x.reshape(-1, x.shape[-1])
     batch, d_in = x2.shape
@@ -222,7 +239,8 @@ def gemv(x: torch.Tensor, W: torch.Tensor, residual: torch.Tensor | None = None,
                             y.data_ptr(), x2.shape[0], x2.shape[1], d_local, _dtype_code(x),
                             _stream(x.device)),
                         local)
-    dev = _need_cuda(x, W, residual, out)
+    dev = _need_cuda(x, W, residual)
+    _check_out(out, dev)
     dt = _dtype_code(x)
     x2 = x.reshape(-1, x.shape[-1])
     batch, d_in = x2.shape
@@ -261,7 +279,8 @@ def flashdecode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     ``seq_lens`` int32 [batch] (device) or None for full length. ``scale``
     defaults to 1/sqrt(128).
     """
-    dev = _need_cuda(q, k_cache, v_cache, seq_lens, page_table, out)
+    dev = _need_cuda(q, k_cache, v_cache, seq_lens, page_table)
+    _check_out(out, dev)
     dt = _dtype_code(q)
     if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
         raise TypeError("q, k_cache and v_cache must share one dtype")

@@ -1,7 +1,9 @@
 /* dbk.h - C ABI of the decodebench_b200 fused decode kernels (sm_100a).
  *
  * Every entry point:
- *   - takes device pointers, sizes and a cudaStream_t passed as void*;
+ *   - takes device pointers, sizes and a cudaStream_t passed as void*; an output
+ *     pointer may also be pinned host memory (its unified address): the kernel
+ *     then writes the result there directly, with no separate copy-out;
  *   - allocates nothing and never synchronises (safe inside CUDA-graph capture);
  *     scratch space is a caller-owned workspace sized by dbk_workspace_bytes();
  *   - returns 0 on success, a negative DBK_E* code for a rejected argument, or a

@@ -291,3 +291,37 @@ def test_stage_copies_between_pinned_host_and_device():
     with pytest.raises(DbkError):
         big = torch.empty(17, dtype=torch.int8, device="cuda")
         ops.stage(big[1:], torch.zeros(16, dtype=torch.int8).pin_memory())   # misaligned
+
+
+@pytest.mark.gpu
+def test_output_straight_into_pinned_host_memory():
+    """out= a pinned CPU tensor: the kernels write the result into host memory
+    directly; equal to the device-output result; pageable CPU out is refused."""
+    import torch
+
+    from decodebench_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(2, 1024, generator=g, device="cuda").half()
+    gam = torch.randn(1024, generator=g, device="cuda").half()
+    Wg = (torch.randn(700, 1024, generator=g, device="cuda") / 32).half()
+    Wu = (torch.randn(700, 1024, generator=g, device="cuda") / 32).half()
+    ref = ops.gateup_swiglu(x, Wg, Wu, gamma=gam)
+    host = torch.empty(2, 700, dtype=torch.float16).pin_memory()
+    ops.gateup_swiglu(x, Wg, Wu, gamma=gam, out=host)
+    torch.cuda.synchronize()
+    assert torch.equal(host, ref.cpu())
+    ref = ops.rmsnorm_gemv(x, gam, Wg)
+    ops.rmsnorm_gemv(x, gam, Wg, out=host)
+    torch.cuda.synchronize()
+    assert torch.equal(host, ref.cpu())
+    q = torch.randn(1, 8, 128, generator=g, device="cuda").half()
+    K = torch.randn(1, 8, 1000, 128, generator=g, device="cuda").half()
+    V = torch.randn(1, 8, 1000, 128, generator=g, device="cuda").half()
+    ref = ops.flashdecode(q, K, V)
+    hq = torch.empty(1, 8, 128, dtype=torch.float16).pin_memory()
+    ops.flashdecode(q, K, V, out=hq)
+    torch.cuda.synchronize()
+    assert torch.equal(hq, ref.cpu())
+    with pytest.raises(RuntimeError, match="pinned"):
+        ops.gemv(x, Wg, out=torch.empty(2, 700, dtype=torch.float16))
