@@ -194,6 +194,8 @@ extern "C" int dbk_comm_open(int rank, int world, void* local_buf, const void* r
     for (int q = 0; q < p; ++q)
       if (std::memcmp(rec[p].uuid, rec[q].uuid, 16) == 0) return DBK_EDEVICE;
   }
+  // One flag slot per CTA: the exchanging grids (at most one CTA per SM) must fit.
+  if (dev.num_sms > dbk::kMaxCtas) return DBK_EDEVICE;
   auto* c = new (std::nothrow) dbk_comm();
   if (!c) return DBK_ESHAPE;
   c->rank = rank;
