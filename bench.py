@@ -208,7 +208,8 @@ class F2(Workload):
 
     def describe(self):
         return {"workload": f"F2 gate+up GEMV -> SwiGLU, x [{self.batch},{self.d_in}] fp16, "
-                            f"Wg/Wu [{self.d_ff},{self.d_in}] fp16 (config C2)",
+                            f"Wg/Wu [{self.d_ff},{self.d_in}] fp16 "
+                            + ("(config C2)" if self.d_ff == 11008 else "(--rows override)"),
                 "global_batch": self.batch, "d_in": self.d_in, "d_ff": self.d_ff,
                 "parallelism": ("single GPU" if self.world == 1 else
                                 f"tp{self.world}: d_ff column-sharded, {self.xname()} of h"),
@@ -294,12 +295,15 @@ class F1(F2):
 
     name = "f1"
 
-    def __init__(self, rank, world, torch, d=4096):
+    def __init__(self, rank, world, torch, d=4096, d_out=None):
         from decodebench_b200 import costs, ops
 
+        d_out = d_out or d
         self.t, self.ops, self.costs = torch, ops, costs
-        self.rank, self.world, self.batch, self.d_in, self.d_ff = rank, world, 1, d, d
-        self.rows = d // world
+        self.rank, self.world, self.batch, self.d_in, self.d_ff = rank, world, 1, d, d_out
+        if d_out % world:
+            raise SystemExit(f"d_out={d_out} does not split over {world} ranks")
+        self.rows = d_out // world
         dev = torch.device("cuda", torch.cuda.current_device())
         g = torch.Generator(device=dev).manual_seed(99 + rank)
         per_rep = self.rows * d * 2
@@ -1048,6 +1052,9 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="f2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="f1/f2 only: output rows instead of the config's (e.g. 14336, the "
+                         "shape of the reference's own published F1/F2 timings)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1096,7 +1103,12 @@ def main() -> int:
     dev_index = torch.cuda.current_device()
 
     sys.path.insert(0, str(ROOT))
-    wl = WORKLOADS[args.workload](rank, world, torch)
+    if args.rows and args.workload == "f2":
+        wl = F2(rank, world, torch, d_ff=args.rows)
+    elif args.rows and args.workload == "f1":
+        wl = F1(rank, world, torch, d_out=args.rows)
+    else:
+        wl = WORKLOADS[args.workload](rank, world, torch)
     if world > 1 and os.environ.get("DBK_EXCHANGE", "peer") != "nccl":
         from decodebench_b200.comm import PeerComm
 
