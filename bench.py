@@ -950,19 +950,24 @@ def _capture(torch, body):
 
 
 class StepGraphs:
-    """CUDA graphs of the step: one graph of `per` consecutive steps (rotating
-    the weight replicas; consecutive kernels overlap prologue and tail through
-    programmatic dependent launch) plus one single-step graph per replica, so
-    that exactly K steps can be replayed."""
+    """CUDA graphs of the step. `prepare(n)` captures one graph of exactly n
+    consecutive steps (rotating the weight replicas; consecutive kernels overlap
+    prologue and tail through programmatic dependent launch), and `run(n)`
+    replays it, so a timed region of K steps is one graph launch whatever K is.
+    Counts above `cap` replay a cap-step graph several times."""
 
-    def __init__(self, torch, wl, with_exchange: bool, per: int = 32):
+    def __init__(self, torch, wl, with_exchange: bool, cap: int = 4096):
         self.torch = torch
+        self.wl = wl
+        self.cap = cap
+        self.graphs = {}
 
         def one(r):
             wl.with_exchange = with_exchange
             wl.run_kernel(r)
             if with_exchange:
                 wl.exchange()
+        self.one = one
 
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
@@ -971,16 +976,26 @@ class StepGraphs:
                 one(r)
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
-        self.per = max(wl.nrep, (per // wl.nrep) * wl.nrep)
-        self.big = _capture(torch, lambda: [one(r % wl.nrep) for r in range(self.per)])
-        self.small = [_capture(torch, lambda r=r: one(r)) for r in range(wl.nrep)]
-        torch.cuda.synchronize()
+
+    def _chunks(self, steps: int) -> list[int]:
+        out = [self.cap] * (steps // self.cap)
+        if steps % self.cap:
+            out.append(steps % self.cap)
+        return out
+
+    def prepare(self, *counts: int) -> None:
+        for steps in counts:
+            for n in self._chunks(steps):
+                if n not in self.graphs:
+                    self.graphs[n] = _capture(
+                        self.torch, lambda n=n: [self.one(r % self.wl.nrep) for r in range(n)])
+        self.torch.cuda.synchronize()
 
     def run(self, steps: int) -> None:
-        for _ in range(steps // self.per):
-            self.big.replay()
-        for i in range(steps % self.per):
-            self.small[i % len(self.small)].replay()
+        for n in self._chunks(steps):
+            if n not in self.graphs:
+                raise RuntimeError(f"no graph of {n} steps captured (call prepare({n}) first)")
+            self.graphs[n].replay()
 
 
 def timed(torch, run, steps: int, warmup: int) -> float:
@@ -1005,10 +1020,17 @@ def loop(fn):
     return run
 
 
-def cpu_time(wl, threads: int, budget_s: float, steps: int | None = None, warmup: int = 1):
-    """Median seconds per CPU step; steps=None -> as many as fit in budget_s."""
-    for _ in range(warmup):
+def cpu_time(wl, threads: int, budget_s: float, steps: int | None = None, warmup: int = 1,
+             min_steps: int = 10):
+    """Median seconds per CPU step; steps=None -> as many as fit in budget_s (at
+    least min_steps)."""
+    # Warm up for at least `warmup` steps and ~1.5 s, so thread pools, page
+    # faults and CPU clock ramp are behind the measured steps.
+    t_warm = time.perf_counter() + 1.5
+    n_warm = 0
+    while n_warm < warmup or time.perf_counter() < t_warm:
         wl.cpu_step(threads)
+        n_warm += 1
     times = []
     t_end = time.perf_counter() + budget_s
     while True:
@@ -1017,7 +1039,7 @@ def cpu_time(wl, threads: int, budget_s: float, steps: int | None = None, warmup
         times.append(time.perf_counter() - t0)
         if steps is not None and len(times) >= steps:
             break
-        if steps is None and time.perf_counter() >= t_end and len(times) >= 3:
+        if steps is None and time.perf_counter() >= t_end and len(times) >= min_steps:
             break
     return statistics.median(times), len(times)
 
@@ -1041,6 +1063,10 @@ def cpu_baseline(wl, threads: int, budget_s: float, steps=None, warmup=1) -> dic
                        f"{'the full step' if frac >= 1 else f'{frac:.3f} of the rows'}; "
                        "weights pre-converted fp16->fp32 once, untimed; median step time, "
                        "GB/s over the same algorithmic fp16 bytes")}
+
+
+# Seconds of CPU work per cpu_baseline measurement (both arms).
+CPU_BUDGET_S = 12.0
 
 
 # ---------------------------------------------------------------- main
@@ -1079,7 +1105,9 @@ def main() -> int:
         torch.set_num_threads(threads)
         wl = WORKLOADS[args.workload].__new__(WORKLOADS[args.workload])
         _cpu_only_init(wl, args.workload, torch)
-        cb = cpu_baseline(wl, threads, budget_s=120.0, steps=args.steps, warmup=args.warmup)
+        # The same sampler, budget and warm-up as the GPU arm's cpu_baseline leg, so
+        # the two CPU numbers describe the same measurement.
+        cb = cpu_baseline(wl, threads, budget_s=CPU_BUDGET_S)
         us = cb["us_per_step"]
         line = {"metric": METRIC, "value": cb["value"], "unit": "GB/s", "impl": "reference",
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -1116,6 +1144,7 @@ def main() -> int:
 
     # --- device-timed value: graphs of kernel + exchange, rotated over replicas
     graphs = StepGraphs(torch, wl, with_exchange=True)
+    graphs.prepare(args.warmup, args.steps, 256)
     sampler = ClockSampler(dev_index)
     sampler.start()
     graphs.run(args.warmup)
@@ -1143,6 +1172,7 @@ def main() -> int:
     # --- kernel-only timing for the roofline (the dominant, and only, kernel)
     if world > 1:
         kgraphs = StepGraphs(torch, wl, with_exchange=False)
+        kgraphs.prepare(args.warmup, args.steps)
         kms = timed(torch, kgraphs.run, args.steps, args.warmup)
     else:
         kms = ms
@@ -1156,7 +1186,10 @@ def main() -> int:
                 else "fallback 6650 GB/s", "kernel_us": round(k_us, 3),
                 "bytes_per_launch": wl.launch_bytes()}
 
-    # --- e2e through the public API with host buffers
+    # --- e2e through the public API with host buffers. Every step stages its input
+    # in from pinned host memory and its result out to pinned host memory. Timed
+    # twice: eagerly (one Python call per op, as a script calls the ops) and as
+    # one CUDA graph of the same K steps (as a decode engine drives them).
     h2d, d2h = wl.e2e_setup()
     host = {}
 
@@ -1165,10 +1198,25 @@ def main() -> int:
         for _ in range(n):
             wl.e2e_step()
         host["us"] = (time.perf_counter() - t0) * 1e6 / max(n, 1)
-    e_ms = timed(torch, e2e_run, args.steps, args.warmup)
+    eager_ms = timed(torch, e2e_run, args.steps, args.warmup)
+    eager_us = eager_ms * 1e3 / args.steps
+    egraphs = {}
+    s_cap = torch.cuda.Stream()
+    s_cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s_cap):
+        wl.e2e_step()
+    torch.cuda.current_stream().wait_stream(s_cap)
+    for n in {args.warmup, args.steps}:
+        egraphs[n] = _capture(torch, lambda n=n: [wl.e2e_step() for _ in range(n)])
+    torch.cuda.synchronize()
+    egraphs[args.warmup].replay()
+    e_ms = timed(torch, lambda n: egraphs[n].replay(), args.steps, 0)
     e_us = e_ms * 1e3 / args.steps
     e2e = {"value": round(wl.step_bytes_total() / (e_us * 1e-6) / 1e9, 1), "unit": "GB/s",
            "us_per_step": round(e_us, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "mode": "one CUDA graph of the K steps, each step: H2D input, op, D2H result",
+           "eager_us_per_step": round(eager_us, 3),
+           "eager_value": round(wl.step_bytes_total() / (eager_us * 1e-6) / 1e9, 1),
            "host_enqueue_us_per_step": round(host.get("us", 0.0), 3),
            "path": "decodebench_b200.ops (ctypes -> libdbk.so C ABI); input in by ops.stage (dbk_copy: a kernel reading the pinned host buffer); at N=1 the batch<=8 ops and FlashDecode write their result straight into a pinned host buffer (out=); otherwise (the MLP's tcgen05 path, N>1) the result goes out by ops.stage"}
 
@@ -1180,7 +1228,7 @@ def main() -> int:
 
             if O.have_ref():
                 torch.set_num_threads(threads)
-                cb = cpu_baseline(wl, threads, budget_s=12.0)
+                cb = cpu_baseline(wl, threads, budget_s=CPU_BUDGET_S)
         line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us_step / 1e3, 6),
                 "us_per_step": round(us_step, 3), "hbm_frac_of_peak": round(value / world / peak, 4),

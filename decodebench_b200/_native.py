@@ -26,6 +26,8 @@ SIGNATURES = {
     "dbk_abi_version": (_I, []),
     "dbk_status_string": (ctypes.c_char_p, [_I]),
     "dbk_take_device_error": (_I, []),
+    "dbk_set_spin_limit": (_I, [ctypes.c_uint32]),
+    "dbk_test_bounded_wait": (_I, [_I, _P]),
     "dbk_workspace_bytes": (_SZ, [_I, _I64, _I64, _I64]),
     "dbk_flashdecode_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "dbk_rmsnorm_gemv": (_I, [_P, _P, _P, _P, _I, _I, _I, _F, _I, _P, _SZ, _P]),

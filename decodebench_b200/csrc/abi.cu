@@ -5,12 +5,14 @@
 #include <mutex>
 #include <vector>
 
+#include "comm.cuh"
 #include "common.cuh"
 #include "dbk_internal.h"
 
 namespace dbk {
 
 __device__ int dbk_device_error = 0;
+__device__ uint32_t dbk_spin_limit = kSpinLimit;
 #ifdef DBK_TRACE
 __device__ unsigned long long dbk_trace[2048 * 16];
 }  // namespace dbk
@@ -184,4 +186,38 @@ extern "C" int dbk_take_device_error(void) {
   e = cudaMemcpyToSymbol(dbk::dbk_device_error, &zero, sizeof(int));
   if (e != cudaSuccess) return (int)e;
   return v;
+}
+
+extern "C" int dbk_set_spin_limit(uint32_t polls) {
+  const uint32_t v = polls == 0 ? dbk::kSpinLimit : polls;
+  return (int)cudaMemcpyToSymbol(dbk::dbk_spin_limit, &v, sizeof(v));
+}
+
+// ---------------------------------------------------------------------------
+// Test hook: one CTA runs the library's own bounded waits on events that never
+// happen, so that a test can watch a wait give up, record its code and return.
+namespace dbk {
+namespace {
+__device__ unsigned long long g_never_set_flag = 0;
+
+__global__ void bounded_wait_probe_kernel(int which) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  if (which == 0) {
+    // An mbarrier expecting one arrival that nobody makes.
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    (void)mbar_wait(&bar, 0, kDevTimeoutFull);
+  } else {
+    // A peer flag that no peer ever raises.
+    (void)wait_flag(&g_never_set_flag, 1ull);
+  }
+}
+}  // namespace
+}  // namespace dbk
+
+extern "C" int dbk_test_bounded_wait(int which, void* stream) {
+  if (which != 0 && which != 1) return DBK_ESHAPE;
+  dbk::bounded_wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(which);
+  return (int)cudaGetLastError();
 }

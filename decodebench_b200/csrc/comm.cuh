@@ -51,8 +51,9 @@ __device__ __forceinline__ char* staging(char* buf, const PeerSet& ps, int parit
 // Bounded wait until *f >= v (acquire); records kDevTimeoutPeer and gives up.
 __device__ __forceinline__ bool wait_flag(const unsigned long long* f, unsigned long long v) {
   uint32_t n = 0;
+  const uint32_t lim = spin_limit();
   while (ld_acquire_sys(f) < v) {
-    if (++n >= kSpinLimit) {
+    if (++n >= lim) {
       record_error(kDevTimeoutPeer);
       return false;
     }

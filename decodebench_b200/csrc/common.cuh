@@ -30,10 +30,16 @@ enum DeviceError : int {
 
 extern __device__ int dbk_device_error;
 
-// Poll budget for every spin-wait: mbarrier.try_wait suspends for a
+// Default poll budget for every spin-wait: mbarrier.try_wait suspends for a
 // hardware-chosen interval per poll, so 1<<24 polls is seconds, far beyond
-// any legitimate wait in these kernels.
+// any legitimate wait in these kernels. The budget in force is dbk_spin_limit
+// (per device, set by dbk_set_spin_limit; tests lower it to make a wait run out).
 constexpr uint32_t kSpinLimit = 1u << 24;
+extern __device__ uint32_t dbk_spin_limit;
+
+__device__ __forceinline__ uint32_t spin_limit() {
+  return *reinterpret_cast<volatile uint32_t*>(&dbk_spin_limit);
+}
 
 __device__ __forceinline__ void record_error(int code) {
   atomicCAS(&dbk_device_error, 0, code);
@@ -113,7 +119,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity to complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err_code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint32_t lim = spin_limit();
+  for (uint32_t i = 1; i < lim; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   record_error(err_code);
   return false;

@@ -775,9 +775,9 @@ extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v
 // variant takes it from a fixed array compiled into the library instead.
 //
 // The array lives in every GPU that loads the library, until the process
-// exits. Its address is looked up once per device (cudaGetSymbolAddress) on
-// the first call made with that device current, so that first call should
-// come before any stream capture. All calls share the one array: calls that
+// exits. Its address is looked up (cudaGetSymbolAddress) on the first call
+// made in each CUDA context, so that first call should come before any stream
+// capture. All calls share the one array: calls that
 // overlap on the GPU (different streams, different threads) race and give
 // wrong results. Each call clears the arrival counters it uses before the
 // kernel runs.
@@ -785,23 +785,66 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = (size_t)2 << 20;   // 2 MiB
 static __device__ __align__(256) uint8_t g_fd_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevicesNoAlloc = 64;
-void* g_fd_scratch_ptr[kMaxDevicesNoAlloc];
+// The array's device address differs per CUDA context: a device's primary
+// context and any context the host creates on it each load their own copy of
+// the module, and a context re-created after cudaDeviceReset loads it anew.
+// The cache is therefore keyed by the context's process-unique id
+// (cuCtxGetId; ids are never reused), not by the device ordinal.
+constexpr int kMaxContextsNoAlloc = 64;
+struct ScratchEntry {
+  unsigned long long ctx_id;
+  void* ptr;
+};
+ScratchEntry g_fd_scratch_cache[kMaxContextsNoAlloc];
+int g_fd_scratch_n = 0;
 std::mutex g_fd_scratch_mu;
 
+// Driver entry points resolved through the runtime (the library does not link
+// libcuda directly, so it still loads on machines without a driver).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+template <typename Fn>
+Fn driver_fn(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<Fn>(p);
+}
+
 int scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return (int)e;
-  if (dev < 0 || dev >= kMaxDevicesNoAlloc) return DBK_EDEVICE;
-  std::lock_guard<std::mutex> lk(g_fd_scratch_mu);
-  if (g_fd_scratch_ptr[dev] == nullptr) {
-    void* p = nullptr;
+  static const CtxGetCurrentFn cu_ctx_get_current = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  static const CtxGetIdFn cu_ctx_get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+  if (!cu_ctx_get_current || !cu_ctx_get_id) return DBK_EDEVICE;
+  CUcontext ctx = nullptr;
+  if (cu_ctx_get_current(&ctx) != CUDA_SUCCESS) return DBK_EDEVICE;
+  void* p = nullptr;
+  cudaError_t e;
+  if (ctx == nullptr) {
+    // No context current yet: the runtime call makes the device's primary
+    // context current (and gives its address of the array).
     e = cudaGetSymbolAddress(&p, g_fd_scratch);
     if (e != cudaSuccess) return (int)e;
-    g_fd_scratch_ptr[dev] = p;
+    if (cu_ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return DBK_EDEVICE;
   }
-  *out = g_fd_scratch_ptr[dev];
+  unsigned long long id = 0;
+  if (cu_ctx_get_id(ctx, &id) != CUDA_SUCCESS) return DBK_EDEVICE;
+  std::lock_guard<std::mutex> lk(g_fd_scratch_mu);
+  for (int i = 0; i < g_fd_scratch_n; ++i)
+    if (g_fd_scratch_cache[i].ctx_id == id) {
+      *out = g_fd_scratch_cache[i].ptr;
+      return DBK_OK;
+    }
+  e = cudaGetSymbolAddress(&p, g_fd_scratch);
+  if (e != cudaSuccess) return (int)e;
+  // A full table (many short-lived contexts) drops the oldest entry.
+  if (g_fd_scratch_n == kMaxContextsNoAlloc) {
+    for (int i = 1; i < kMaxContextsNoAlloc; ++i) g_fd_scratch_cache[i - 1] = g_fd_scratch_cache[i];
+    --g_fd_scratch_n;
+  }
+  g_fd_scratch_cache[g_fd_scratch_n++] = {id, p};
+  *out = p;
   return DBK_OK;
 }
 }  // namespace

@@ -509,7 +509,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       if (etid == 0) {
         uint32_t n = 0;
         while (ld_acquire_gpu(&a.done[nt]) < ncon) {
-          if (++n >= kSpinLimit) { record_error(kDevTimeoutMerge); break; }
+          if (++n >= spin_limit()) { record_error(kDevTimeoutMerge); break; }
           __nanosleep(64);
         }
       }

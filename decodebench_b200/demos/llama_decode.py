@@ -184,18 +184,48 @@ def _build_layer(dim: int, batch: int, gen):
     def q_rot(qkv, cos, sin):
         return _rot(qkv[:, :H * D].reshape(-1, H, D), cos, sin).contiguous()
 
+    # Attention over the cache plus the new token, one op per stage so the byte
+    # model sees every tensor (the grouped einsums read each kv head once for its
+    # G = H / Hkv query heads, as the fused kernel does).
+    G = H // Hkv
+
     @seq.stage
-    def attn(q_rot, qkv, Kc, Vc, cos, sin):
-        B = q_rot.shape[0]
-        k_new = _rot(qkv[:, H * D:(H + Hkv) * D].reshape(B, Hkv, D), cos, sin)
-        v_new = qkv[:, (H + Hkv) * D:].reshape(B, Hkv, D)
-        K = torch.cat([Kc[:, :, :L], k_new[:, :, None]], dim=2)       # [B, Hkv, L+1, D]
-        V = torch.cat([Vc[:, :, :L], v_new[:, :, None]], dim=2)
-        K = K.repeat_interleave(H // Hkv, dim=1)
-        V = V.repeat_interleave(H // Hkv, dim=1)
-        s = torch.einsum("bhd,bhld->bhl", q_rot.float(), K.float()) / math.sqrt(D)
-        p = torch.softmax(s, dim=-1)
-        return torch.einsum("bhl,bhld->bhd", p, V.float()).half().reshape(B, H * D)
+    def k_rot(qkv, cos, sin):
+        return _rot(qkv[:, H * D:(H + Hkv) * D].reshape(-1, Hkv, D), cos, sin).contiguous()
+
+    @seq.stage
+    def v_new(qkv):
+        return qkv[:, (H + Hkv) * D:].reshape(-1, Hkv, D).contiguous()
+
+    @seq.stage
+    def K_all(k_rot, Kc):
+        return torch.cat([Kc[:, :, :L], k_rot[:, :, None]], dim=2)      # [B, Hkv, L+1, D]
+
+    @seq.stage
+    def V_all(v_new, Vc):
+        return torch.cat([Vc[:, :, :L], v_new[:, :, None]], dim=2)
+
+    @seq.stage
+    def scores(q_rot, K_all):
+        qg = q_rot.reshape(q_rot.shape[0], Hkv, G, D)
+        return torch.einsum("bkgd,bkld->bkgl", qg, K_all).contiguous()  # fp16, fp32 accumulate
+
+    @seq.stage
+    def logits(scores):
+        return scores.to(torch.float32).mul_(1.0 / math.sqrt(D))
+
+    @seq.stage
+    def probs(logits):
+        return torch.softmax(logits, dim=-1)
+
+    @seq.stage
+    def p_half(probs):
+        return probs.half()
+
+    @seq.stage
+    def attn(p_half, V_all):
+        o = torch.einsum("bkgl,bkld->bkgd", p_half, V_all)
+        return o.reshape(o.shape[0], H * D)
 
     @seq.stage
     def o_proj(attn, Wo):

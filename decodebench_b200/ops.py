@@ -464,5 +464,30 @@ def stage(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
 
 
 def take_device_error() -> int:
-    """Error code a kernel recorded after a bounded wait gave up (0 = none); clears it."""
-    return N.load().dbk_take_device_error()
+    """Error code a kernel recorded after a bounded wait gave up (0 = none); clears it.
+
+    A kernel that gave up may have left arrival counters of its workspace
+    non-zero (a partial it never merged), so on a non-zero code the cached
+    workspaces are dropped: later calls start from fresh zero-filled ones.
+    Synchronises the current device."""
+    code = N.load().dbk_take_device_error()
+    if code != 0:
+        with _ws_lock:
+            _ws_cache.clear()
+    return code
+
+
+def check_device_error() -> None:
+    """Raise RuntimeError if a kernel recorded a bounded-wait failure since the last
+    check (see :func:`take_device_error`); synchronises the current device."""
+    code = take_device_error()
+    if code > 0 and code < 16:
+        raise RuntimeError(f"a decodebench_b200 kernel gave up a bounded wait (device error {code}); "
+                           "its outputs are not valid")
+    if code != 0:
+        raise RuntimeError(f"dbk_take_device_error failed: {N.load().dbk_status_string(code)!r}")
+
+
+def set_spin_limit(polls: int = 0) -> None:
+    """Poll budget of the kernels' bounded waits on the current device (0 = default)."""
+    N.check("set_spin_limit", N.load().dbk_set_spin_limit(int(polls)))

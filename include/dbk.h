@@ -57,6 +57,21 @@ const char* dbk_status_string(int status);
  * clear it. Synchronises the current device. */
 int dbk_take_device_error(void);
 
+/* Poll budget of every bounded wait in this library's kernels, for the current
+ * device (0 restores the default of 1<<24 polls, seconds). No counterpart in
+ * the reference: the reference's kernels have no bounded waits. A smaller
+ * budget lets a test make a wait give up quickly; set it only while no kernel
+ * of this library is running on the device. Synchronous. */
+int dbk_set_spin_limit(uint32_t polls);
+
+/* Test hook (no counterpart in the reference): launches one CTA that runs the
+ * library's bounded wait on an event that never happens -- which = 0: an
+ * mbarrier nobody arrives at (records 1, "stage never filled"); which = 1: a
+ * peer flag nobody raises (records 5, "peer signal missing"). The kernel gives
+ * up after the spin budget, records the code for dbk_take_device_error and
+ * returns, leaving the context usable. */
+int dbk_test_bounded_wait(int which, void* stream);
+
 /* Workspace bytes a GEMV-family operation needs (0 if none):
  *   op = DBK_OP_RMSNORM_GEMV | DBK_OP_GATEUP_SWIGLU | DBK_OP_GEMV,
  *   sizes (batch, d_in, d_out or d_ff).
@@ -140,8 +155,9 @@ int dbk_flashdecode(const void* q, const void* k_cache, const void* v_cache,
  * the scratch comes from a 2 MiB array compiled into the library and held on
  * every GPU that loads it until the process exits. Sizes whose workspace
  * (dbk_flashdecode_workspace_bytes) exceeds 2 MiB return DBK_EWORKSPACE.
- * The first call on a device looks up the array's device address and should
- * come before any stream capture. All calls share the array: calls that
+ * The first call in each CUDA context (a device's primary context, or a
+ * context the host made current) looks up the array's device address in that
+ * context and should come before any stream capture. All calls share the array: calls that
  * overlap on the GPU race. Allocates nothing. */
 int dbk_flashdecode_noalloc(const void* q, const void* k_cache, const void* v_cache,
                             const int32_t* page_table, const int32_t* seq_lens, void* out,

@@ -12,6 +12,7 @@ between float32 and fp16/bf16 with round-to-nearest-even.
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 from pathlib import Path
 
@@ -72,13 +73,21 @@ def _bind(path: Path, sigs: dict) -> ctypes.CDLL:
     return lib
 
 
+def reference_root() -> Path:
+    """The reference checkout: $DBK_REFERENCE_ROOT, else a `reference` directory
+    beside this repository's root."""
+    env = os.environ.get("DBK_REFERENCE_ROOT")
+    return Path(env) if env else HERE.parent.parent / "reference"
+
+
 def build(ref: bool = True) -> None:
     """Compile the oracle (and the reference's CPU library when its sources exist)."""
     targets = ["oracle"]
-    ref_src = Path("/root/reference/validation/src/reference/cpu_reference.cpp")
+    root = reference_root()
+    ref_src = root / "validation/src/reference/cpu_reference.cpp"
     if ref and ref_src.exists():
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", str(HERE), *targets], check=True)
+    subprocess.run(["make", "-s", "-C", str(HERE), *targets, f"REF={root}"], check=True)
 
 
 def lib() -> ctypes.CDLL:

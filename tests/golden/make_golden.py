@@ -1,6 +1,7 @@
 """Generate golden fixtures from the reference's own PyTorch stage code (CPU).
 
-Run in a container that has the reference checkout (default /root/reference):
+Run where the reference checkout is present ($DBK_REFERENCE_ROOT, else a
+``reference`` directory beside this repository):
 
     python tests/golden/make_golden.py [--ref /path/to/Decodebench]
 
@@ -16,6 +17,7 @@ inputs. Inputs and outputs are stored as raw 16-bit patterns in
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -50,11 +52,15 @@ def _h(rng, shape, scale=1.0):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=None,
+                    help="reference checkout (default: $DBK_REFERENCE_ROOT, else ../reference "
+                         "beside this repository)")
     args = ap.parse_args()
     import torch
 
-    chains = _load_reference(Path(args.ref))
+    ref = args.ref or os.environ.get("DBK_REFERENCE_ROOT") or str(
+        Path(__file__).resolve().parents[3] / "reference")
+    chains = _load_reference(Path(ref))
     rng = np.random.default_rng(42)
     T = torch.from_numpy
     cases = {}
