@@ -12,13 +12,21 @@
 namespace dbk {
 
 __device__ int dbk_device_error = 0;
-__device__ uint32_t dbk_spin_limit = kSpinLimit;
+__constant__ uint32_t dbk_spin_limit = kSpinLimit;
 #ifdef DBK_TRACE
-__device__ unsigned long long dbk_trace[2048 * 16];
+__device__ unsigned long long dbk_trace[4 * 2048 * 16];
+__device__ unsigned int dbk_trace_ticket;
 }  // namespace dbk
-// Development builds only: copies the phase timestamps to the host.
+// Development builds only: copies the phase timestamps to the host / clears them.
 extern "C" int dbk_trace_read(void* host, size_t bytes) {
   return (int)cudaMemcpyFromSymbol(host, dbk::dbk_trace, bytes);
+}
+extern "C" int dbk_trace_clear(void) {
+  static unsigned long long zeros[4 * 2048 * 16];
+  unsigned int z = 0;
+  cudaError_t e = cudaMemcpyToSymbol(dbk::dbk_trace, zeros, sizeof(zeros));
+  if (e != cudaSuccess) return (int)e;
+  return (int)cudaMemcpyToSymbol(dbk::dbk_trace_ticket, &z, sizeof(z));
 }
 namespace dbk {
 #endif
@@ -126,13 +134,15 @@ int encode_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t inner
   return r == CUDA_SUCCESS ? DBK_OK : DBK_ESHAPE;
 }
 
-int encode_tmap_kv3d(CUtensorMap* out, const void* base, int dtype, uint64_t rows) {
+int encode_tmap_kv3d(CUtensorMap* out, const void* base, int dtype, uint64_t rows,
+                     uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return (int)cudaErrorNotSupported;
   if (!aligned16(base)) return DBK_EALIGN;
   const cuuint64_t dims[3] = {64, rows, 2};
   const cuuint64_t strides[2] = {256, 128};
-  const cuuint32_t box[3] = {64, 16, 2};
+  if (box_rows < 8 || box_rows > 256) return DBK_ESHAPE;
+  const cuuint32_t box[3] = {64, box_rows, 2};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(out, dtype == DBK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                   3, const_cast<void*>(base), dims, strides, box, estr,

@@ -35,11 +35,11 @@ extern __device__ int dbk_device_error;
 // any legitimate wait in these kernels. The budget in force is dbk_spin_limit
 // (per device, set by dbk_set_spin_limit; tests lower it to make a wait run out).
 constexpr uint32_t kSpinLimit = 1u << 24;
-extern __device__ uint32_t dbk_spin_limit;
+// Constant memory: read through the constant cache, so a wait loop pays no
+// global-memory latency for it.
+extern __constant__ uint32_t dbk_spin_limit;
 
-__device__ __forceinline__ uint32_t spin_limit() {
-  return *reinterpret_cast<volatile uint32_t*>(&dbk_spin_limit);
-}
+__device__ __forceinline__ uint32_t spin_limit() { return dbk_spin_limit; }
 
 __device__ __forceinline__ void record_error(int code) {
   atomicCAS(&dbk_device_error, 0, code);
@@ -59,26 +59,44 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // Phase timestamps for development builds (-DDBK_TRACE) only; compiled out of
 // the library. Slot k of CTA c is written to dbk_trace[c * 16 + k].
 #ifdef DBK_TRACE
-extern __device__ unsigned long long dbk_trace[2048 * 16];
+// Four launches are kept apart: every CTA takes a ticket at its start (the
+// CTAs of launch n all start before those of launch n + 1 can), and launch
+// (ticket / gridDim.x) % 4 picks the buffer.
+extern __device__ unsigned long long dbk_trace[4 * 2048 * 16];
+extern __device__ unsigned int dbk_trace_ticket;
+__device__ __forceinline__ int& trace_launch() {
+  __shared__ int s_launch;
+  return s_launch;
+}
+#define DBK_TRACE_BEGIN()                                                          \
+  do {                                                                             \
+    if (threadIdx.x == 0)                                                          \
+      dbk::trace_launch() = (int)((atomicAdd(&dbk::dbk_trace_ticket, 1u) / gridDim.x) & 3); \
+  } while (0)
+#define DBK_TRACE_SLOT(slot) \
+  dbk::dbk_trace[((size_t)dbk::trace_launch() * 2048 + blockIdx.x) * 16 + (slot)]
 #define DBK_MARK(cond, slot)                                              \
   do {                                                                    \
     if (cond) {                                                           \
       unsigned long long t_;                                              \
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));              \
-      dbk::dbk_trace[blockIdx.x * 16 + (slot)] = t_;                      \
+      DBK_TRACE_SLOT(slot) = t_;                                          \
     }                                                                     \
   } while (0)
-// Adds the time spent in a wait to dbk_trace[blockIdx.x * 16 + slot] (cond threads only).
+// Adds the time spent in a wait to slot `slot` (cond threads only).
 #define DBK_TIMED_WAIT(cond, slot, expr)                                  \
   ([&]() {                                                                \
     unsigned long long a_, b_;                                            \
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(a_));                \
     const bool r_ = (expr);                                               \
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(b_));                \
-    if (cond) dbk::dbk_trace[blockIdx.x * 16 + (slot)] += b_ - a_;        \
+    if (cond) DBK_TRACE_SLOT(slot) += b_ - a_;                            \
     return r_;                                                            \
   }())
 #else
+#define DBK_TRACE_BEGIN() \
+  do {                    \
+  } while (0)
 #define DBK_TIMED_WAIT(cond, slot, expr) (expr)
 #define DBK_MARK(cond, slot) \
   do {                       \

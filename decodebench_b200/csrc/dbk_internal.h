@@ -42,11 +42,13 @@ int encode_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t inner
                    bool swizzle128);
 
 // 3-D tiled TMA descriptor viewing a row-major [rows, 128] matrix of 16-bit
-// elements as [2 halves][rows][64] (strides 128 B and 256 B): one box (16 rows x
-// both halves) reads 16 whole 256-byte rows (4 KB) and lands as 32 swizzled
-// 128-byte lines, line = 16 * half + row, so 8 consecutive rows of one half
-// occupy 8 different swizzle phases (conflict-free ldmatrix).
-int encode_tmap_kv3d(CUtensorMap* out, const void* base, int dtype, uint64_t rows);
+// elements as [2 halves][rows][64] (strides 128 B and 256 B): one box (box_rows
+// rows x both halves) reads box_rows whole 256-byte rows (box_rows * 256 bytes in
+// one copy) and lands as 2 * box_rows swizzled 128-byte lines,
+// line = box_rows * half + row, so 8 consecutive rows of one half occupy 8
+// different swizzle phases (conflict-free ldmatrix).
+int encode_tmap_kv3d(CUtensorMap* out, const void* base, int dtype, uint64_t rows,
+                     uint32_t box_rows);
 
 // Launch `func(*args)` (one by-value struct parameter) with programmatic
 // dependent launch enabled unless DBK_PDL=0 is set in the environment.

@@ -47,7 +47,7 @@ constexpr int kWarps = 8;
 constexpr int kConsumers = kWarps * 32;
 constexpr int kThreads = kConsumers + 32;
 constexpr int kMaxStages = 6;
-constexpr int kBoxRows = 16;            // TMA box height (tokens) on the tensor-core path
+constexpr int kMinBoxRows = 16;         // smallest TMA box height (tokens) on the tensor-core path
 constexpr int kMaxBatchSmem = 1024;     // sequences whose tile offsets live in shared memory
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMrg = kD + 4;            // merge-row stride: o[128], m, l, pad (16-byte rows)
@@ -67,7 +67,16 @@ struct FdArgs {
   int batch, hq, hkv, max_len, page_size, max_pages;
   float qscale;           // scale * log2(e)
   int nstages;
+  int box_shift;          // tensor-core path: log2 of the TMA box height (16, 32 or 64 tokens)
 };
+
+// Shared-memory line (128 bytes) holding dims [64 h, 64 h + 64) of token `tok` of
+// a stage on the tensor-core path: boxes of 2^sh tokens land one after another,
+// each as [half][row] lines. The 128-byte swizzle phase of a line is its index
+// mod 8 = tok mod 8, so the 8 rows of an ldmatrix block never share banks.
+__device__ __forceinline__ int kv_line(int tok, int h, int sh) {
+  return ((tok >> sh) << (sh + 1)) + (h << sh) + (tok & ((1 << sh) - 1));
+}
 
 __device__ __forceinline__ int seq_len(const FdArgs& a, int b) {
   return a.lens ? min(max(a.lens[b], 0), a.max_len) : a.max_len;
@@ -145,6 +154,74 @@ __device__ __forceinline__ int range_start(int64_t c, int64_t T, int64_t grid) {
   return (int)(c * T / grid);
 }
 
+// Arrival at a row's counter: releases this CTA's partial (the caller's
+// barrier orders every consumer thread's partial stores before it). Nothing
+// comes back, so the CTA does not wait on the round trip.
+__device__ __forceinline__ void arrive_release(int* p) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p) : "memory");
+}
+
+// Bounded wait (acquire) until *p == v; records kDevTimeoutMerge and gives up.
+__device__ __forceinline__ bool wait_count(const int* p, int v) {
+  uint32_t n = 0;
+  const uint32_t lim = spin_limit();
+  while (ld_acquire_gpu(p) != v) {
+    if (++n >= lim) {
+      record_error(kDevTimeoutMerge);
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return true;
+}
+
+// Log-sum-exp merge of row (b, hk)'s partials (reference f4_reduce_kernel,
+// validation/src/kernels/fused/f4.cu:294-319), by the consumer threads of the
+// CTA that holds the row's last tile, once the others have arrived: M = max_c m_c, out = sum_c 2^(m_c - M) o_c /
+// sum_c 2^(m_c - M) l_c (m in log2 units), contributors in CTA order (results do
+// not depend on timing). Every thread loads up to 8 contributors' (m, l, o) at
+// once and rescales its running sums per batch of 8, so a merge costs about one
+// L2 round trip per 8 contributors.
+template <typename T, int G>
+__device__ void merge_row(const FdArgs& a, int b, int hk, int rs, int ntb, int64_t Ttot,
+                          int grid, int tid) {
+  T* out = static_cast<T*>(a.out);
+  const int c_first = owner(rs, Ttot, grid), c_last = owner(rs + ntb - 1, Ttot, grid);
+  const int np = c_last - c_first + 1;
+  for (int idx = tid; idx < G * kD; idx += kConsumers) {
+    const int g = idx / kD, d = idx - g * kD;
+    float M = -INFINITY, L = 0.f, O = 0.f;
+    for (int c0 = 0; c0 < np; c0 += 8) {
+      float mc[8], lc[8], oc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        mc[k] = -INFINITY; lc[k] = 0.f; oc[k] = 0.f;
+        if (c0 + k < np) {
+          const int c = c_first + c0 + k;
+          const int sl = 2 * c + (range_start(c, Ttot, grid) >= rs ? 0 : 1);
+          const float2 ml = __ldcg(&a.part_ml[(size_t)sl * G + g]);
+          mc[k] = ml.x; lc[k] = ml.y;
+          oc[k] = __ldcg(&a.part_o[((size_t)sl * G + g) * kD + d]);
+        }
+      }
+      float Mn = M;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) Mn = fmaxf(Mn, mc[k]);
+      const float sc = (M == -INFINITY) ? 0.f : exp2f(M - Mn);
+      L *= sc;
+      O *= sc;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float f = (lc[k] > 0.f) ? exp2f(mc[k] - Mn) : 0.f;
+        L = fmaf(f, lc[k], L);
+        O = fmaf(f, oc[k], O);
+      }
+      M = Mn;
+    }
+    out[((size_t)b * a.hq + (size_t)hk * G + g) * kD + d] = Elem<T>::from_f(O / L);
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 template <typename T, int G, bool kMma>
 __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_constant__ FdArgs a) {
@@ -155,9 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
   uint64_t* empty = full + a.nstages;
   float* mrg = reinterpret_cast<float*>(empty + a.nstages);              // [kWarps][G][kMrg]
   int* tile0 = reinterpret_cast<int*>(mrg + kWarps * G * kMrg);           // [batch + 1]
-  __shared__ int s_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  DBK_TRACE_BEGIN();
   DBK_MARK(tid == 0, 0);
   if (tid == 0) {
     // A stage is released by every consumer warp (CUDA-core path) or by the
@@ -190,6 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
   const int grid = (int)min((int64_t)gridDim.x, Ttot);
   const int u0 = range_start(blockIdx.x, Ttot, grid);
   const int u1 = range_start(blockIdx.x + 1, Ttot, grid);
+  __shared__ int s_last;
 
   if (warp == kWarps) {
     // ------------------------------------------------------------ producer
@@ -202,7 +280,8 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
     }
     const T* K = static_cast<const T*>(a.k);
     const T* V = static_cast<const T*>(a.v);
-    const bool boxed = (a.pages == nullptr) || (a.page_size % kBoxRows == 0);
+    const bool boxed = (a.pages == nullptr) || (a.page_size % kMinBoxRows == 0);
+    const int br = 1 << a.box_shift;          // tokens per TMA box (tensor-core path)
     if (!boxed) {
       // page_size not a multiple of 16 (CUDA-core path only): page runs one by one
       if (lane != 0) return;
@@ -237,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
 #pragma unroll
         for (int bx = 0; bx < 4; ++bx) {
           int run;
-          if (bx * kBoxRows < n_l) r_l[bx] = kv_rowidx(a, w.b, w.hk, w.tt * kTile + bx * kBoxRows, &run);
+          if (bx * br < n_l) r_l[bx] = kv_rowidx(a, w.b, w.hk, w.tt * kTile + bx * br, &run);
         }
       }
       const int cnt = min(32, u1 - g0);
@@ -256,24 +335,26 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
           else {
             uint8_t* dk = smem + (size_t)s * kStage;
             uint8_t* dv = dk + kStage / 2;
-            const int boxes = (n + kBoxRows - 1) / kBoxRows;
             if constexpr (kMma) {
-              // boxes of 16 tokens x 64 dims; both dim halves of K and of V
-              mbar_arrive_expect_tx(&full[s], (uint32_t)(boxes * 4 * kBoxRows * 128));
+              // boxes of br tokens x both dim halves, for K and for V (one 16 KB copy
+              // each when a box covers the whole 64-token tile)
+              const int boxes = (n + br - 1) / br;
+              mbar_arrive_expect_tx(&full[s], (uint32_t)(boxes * br * 512));
 #pragma unroll
               for (int bx = 0; bx < 4; ++bx) {
                 if (bx >= boxes) break;
-                tma_load_3d(dk + bx * kBoxRows * 256, &a.kmap, 0, (int)r[bx], 0, &full[s], pol);
-                tma_load_3d(dv + bx * kBoxRows * 256, &a.vmap, 0, (int)r[bx], 0, &full[s], pol);
+                tma_load_3d(dk + bx * br * 256, &a.kmap, 0, (int)r[bx], 0, &full[s], pol);
+                tma_load_3d(dv + bx * br * 256, &a.vmap, 0, (int)r[bx], 0, &full[s], pol);
               }
             } else {
+              const int boxes = (n + kMinBoxRows - 1) / kMinBoxRows;
               mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * n * kD * sizeof(T)));
 #pragma unroll
               for (int bx = 0; bx < 4; ++bx) {
                 if (bx >= boxes) break;
-                const int m = min(kBoxRows, n - bx * kBoxRows);
+                const int m = min(kMinBoxRows, n - bx * kMinBoxRows);
                 const uint32_t bytes = (uint32_t)(m * kD * sizeof(T));
-                const size_t so = (size_t)bx * kBoxRows * kD * sizeof(T);
+                const size_t so = (size_t)bx * kMinBoxRows * kD * sizeof(T);
                 bulk_g2s(dk + so, K + r[bx] * kD, bytes, &full[s], pol);
                 bulk_g2s(dv + so, V + r[bx] * kD, bytes, &full[s], pol);
               }
@@ -308,6 +389,10 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
 
   TileWalker w(a, tile0, u0);
   int seg_first = u0;
+  // The split row whose last tile this CTA holds (at most one: a range's first
+  // segment). This CTA merges it after its own tiles, so the merge never stalls
+  // the stream; the row's other contributors only announce their partials.
+  int pend_b = -1, pend_hk = 0, pend_rs = 0, pend_ntb = 0, pend_np = 0;
   for (int u = u0, j = 0; u < u1; ++u, ++j, w.next()) {
     const int s = j % a.nstages;
     const bool seg_begin = (u == u0) || (w.tt == 0);
@@ -357,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             // but the rows may hold stale or out-of-sequence data)
             for (int r = max(n, t0); r < t0 + 16; ++r) {
               uint8_t* p0 = smem + (size_t)s * kStage + kStage / 2 +
-                            ((r >> 4) * 32 + (lane >> 4) * 16 + (r & 15)) * 128;
+                            kv_line(r, lane >> 4, a.box_shift) * 128;
               reinterpret_cast<uint4*>(p0)[lane & 7] = make_uint4(0, 0, 0, 0);
             }
             fence_proxy_async_smem();   // order these writes before the next TMA refill
@@ -372,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             int run;
             const int64_t rr = kv_rowidx(a, w.b, w.hk, w.tt * kTile + tok, &run);
             const T* src = static_cast<const T*>(lane < 16 ? a.k : a.v) + rr * kD + cc * 8;
-            const int line = (tok >> 4) * 32 + (cc >> 3) * 16 + (tok & 15);
+            const int line = kv_line(tok, cc >> 3, a.box_shift);
             uint8_t* dst = smem + (size_t)s * kStage + (lane < 16 ? 0 : kStage / 2) + line * 128 +
                            (((cc & 7) ^ (line & 7)) << 4);
             *reinterpret_cast<uint4*>(dst) = __ldcg(reinterpret_cast<const uint4*>(src));
@@ -388,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             for (int kk = 0; kk < 8; ++kk) {
               const int chunk = 2 * kk + (lane >> 4);     // 16-byte chunk of the 256-byte row
               const int h = chunk >> 3, c = chunk & 7;
-              const int line = (tok >> 4) * 32 + h * 16 + (tok & 15);
+              const int line = kv_line(tok, h, a.box_shift);
               uint32_t ka[4];
               ldsm_x4(kst + line * 128 + ((c ^ (line & 7)) << 4), ka);
               Mma<T>::run((kk & 1) ? sb : sa, ka[0], ka[1], ka[2], ka[3], qa[kk][0], qa[kk][1]);
@@ -441,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
             for (int mt = 0; mt < 8; ++mt) {        // 16-dim m-tiles
               const int chunk = 2 * mt + ((lane >> 3) & 1);
               const int h = chunk >> 3, c = chunk & 7;
-              const int line = (tok >> 4) * 32 + h * 16 + (tok & 15);
+              const int line = kv_line(tok, h, a.box_shift);
               uint32_t va[4];
               ldsm_x4_t(vst + line * 128 + ((c ^ (line & 7)) << 4), va);
               float* d = &o[4 * mt];
@@ -588,58 +673,24 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
     }
     if (whole) continue;
 
-    // ---- publish the partial; the last CTA of this row to arrive merges them
-    __threadfence();
+    // ---- publish the partial: the barrier orders every thread's partial stores
+    // before thread 0's release. The CTA with the row's last tile merges it.
     named_bar_sync(1, kConsumers);
-    const int row_end = rs + w.ntb - 1;
-    const int c_first = owner(rs, Ttot, grid), c_last = owner(row_end, Ttot, grid);
-    if (tid == 0) {
-      const int prev = atomicAdd(&a.done[w.row()], 1);
-      s_last = (prev == c_last - c_first);
+    if (w.tt == w.ntb - 1) {
+      pend_b = w.b; pend_hk = w.hk; pend_rs = rs; pend_ntb = w.ntb;
+      pend_np = owner(rs + w.ntb - 1, Ttot, grid) - owner(rs, Ttot, grid) + 1;
+    } else if (tid == 0) {
+      arrive_release(&a.done[w.row()]);
     }
+  }
+  if (pend_b >= 0) {
+    // Every other contributor announces exactly once; all CTAs of the grid are
+    // resident together (one per SM, grid <= SM count), so the wait ends.
+    int* cnt = &a.done[pend_b * a.hkv + pend_hk];
+    if (tid == 0) s_last = wait_count(cnt, pend_np - 1) ? 1 : 0;
     named_bar_sync(1, kConsumers);
-    if (!s_last) continue;
-    __threadfence();
-    {
-      // Merge the row's partials: (m, l) of every contributor loaded in parallel
-      // into shared memory (mrg is free again), weights computed once per head,
-      // then every thread sums its output elements with independent loads.
-      const int np = c_last - c_first + 1;
-      float* wm = mrg;                          // [np][G]: m, then the weight e^(m - M)
-      float* wl = mrg + np * G;                 // [np][G]: l
-      float* inv_l = wl + np * G;               // [G]
-      int* slot_of = reinterpret_cast<int*>(inv_l + G);   // [np]
-      for (int i = tid; i < np * G; i += kConsumers) {
-        const int c = c_first + i / G, g = i % G;
-        const int sl = 2 * c + (range_start(c, Ttot, grid) >= rs ? 0 : 1);
-        if (g == 0) slot_of[i / G] = sl;
-        const float2 ml = __ldcg(&a.part_ml[(size_t)sl * G + g]);
-        wm[i] = ml.x;
-        wl[i] = ml.y;
-      }
-      named_bar_sync(1, kConsumers);
-      if (tid < G) {
-        float M = -INFINITY;
-        for (int c = 0; c < np; ++c) M = fmaxf(M, wm[c * G + tid]);
-        float L = 0.f;
-        for (int c = 0; c < np; ++c) {
-          const float f = exp2f(wm[c * G + tid] - M);
-          wm[c * G + tid] = f;
-          L = fmaf(f, wl[c * G + tid], L);
-        }
-        inv_l[tid] = 1.f / L;
-      }
-      named_bar_sync(1, kConsumers);
-      for (int idx = tid; idx < G * kD; idx += kConsumers) {
-        const int g = idx / kD, d = idx - g * kD;
-        float O = 0.f;
-#pragma unroll 4
-        for (int c = 0; c < np; ++c)
-          O = fmaf(wm[c * G + g], __ldcg(&a.part_o[((size_t)slot_of[c] * G + g) * kD + d]), O);
-        out[((size_t)w.b * a.hq + (size_t)w.hk * G + g) * kD + d] = Elem<T>::from_f(O * inv_l[g]);
-      }
-    }
-    if (tid == 0) a.done[w.row()] = 0;   // ready for the next launch
+    if (s_last) merge_row<T, G>(a, pend_b, pend_hk, pend_rs, pend_ntb, Ttot, grid, tid);
+    if (tid == 0) *cnt = 0;                   // ready for the next launch
     DBK_MARK(tid == 0, 7);
   }
   DBK_MARK(tid == 0, 6);
@@ -649,7 +700,7 @@ size_t ws_bytes_for(int grid, int batch, int hq, int hkv) {
   const int G = hq / hkv;
   size_t b = (size_t)2 * grid * G * kD * sizeof(float);   // part_o
   b += (size_t)2 * grid * G * sizeof(float2);             // part_ml
-  b += (size_t)batch * hkv * sizeof(int);                 // done counters
+  b += (size_t)batch * hkv * sizeof(int);                 // arrival counters
   return (b + 255) & ~(size_t)255;
 }
 
@@ -717,7 +768,7 @@ extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v
     if (page_size < 1 || max_pages_per_seq < 1 ||
         (int64_t)page_size * max_pages_per_seq < max_len)
       return DBK_ESHAPE;
-    if (G >= 4 && page_size % kBoxRows != 0) return DBK_ESHAPE;
+    if (G >= 4 && page_size % kMinBoxRows != 0) return DBK_ESHAPE;
   }
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
     return DBK_EALIGN;
@@ -746,18 +797,22 @@ extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v
   a.qscale = scale * kLog2e;
   // Tensor-core path whenever 16-token TMA boxes stay inside pages; CUDA cores
   // otherwise (page sizes that are not multiples of 16, G <= 2 only).
-  const bool mma = (page_table == nullptr) || (page_size % kBoxRows == 0);
+  const bool mma = (page_table == nullptr) || (page_size % kMinBoxRows == 0);
+  // TMA box height: a whole 64-token tile per copy (16 KB of K, 16 KB of V) for
+  // contiguous caches, where copies of 16 KB stream near the HBM rate and 4 KB
+  // copies do not; 16 tokens (4 KB) for paged caches.
+  a.box_shift = (mma && page_table == nullptr) ? 6 : 4;
   if (mma) {
     // 2-D views [rows, 128] of the caches for the tensor-core path's TMA boxes.
     // Contiguous caches: exact extent, so a box overhanging the end of the cache
     // reads zeros. Paged caches: the page count is not an argument; every box
-    // (16 rows, page_size % 16 == 0, box-aligned within its page) stays inside
+    // (box_rows dividing page_size, box-aligned within its page) stays inside
     // one page of the table, so the view's extent only needs to cover them.
     const uint64_t prow = page_table ? (((uint64_t)1 << 31) - 1)
                                      : (uint64_t)batch * n_kv_heads * max_len;
-    rc = encode_tmap_kv3d(&a.kmap, k_cache, dtype, prow);
+    rc = encode_tmap_kv3d(&a.kmap, k_cache, dtype, prow, 1u << a.box_shift);
     if (rc) return rc;
-    rc = encode_tmap_kv3d(&a.vmap, v_cache, dtype, prow);
+    rc = encode_tmap_kv3d(&a.vmap, v_cache, dtype, prow, 1u << a.box_shift);
     if (rc) return rc;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -861,7 +916,8 @@ extern "C" int dbk_flashdecode_noalloc(const void* q, const void* k_cache, const
   void* ws = nullptr;
   int rc = scratch_address(&ws);
   if (rc) return rc;
-  // The arrival counters sit at the end of the workspace layout; start them at zero.
+  // The arrival counters sit after the partials; the array may hold another
+  // shape's partials there from an earlier call, so start them at zero.
   const size_t counters = (size_t)batch * n_kv_heads * sizeof(int);
   const size_t G = (size_t)(n_q_heads / n_kv_heads);
   DeviceInfo dev;

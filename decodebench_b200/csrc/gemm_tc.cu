@@ -221,6 +221,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   __shared__ float xbuf[kMaxRows / 2][17];    // lo-row exchange (split)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  DBK_TRACE_BEGIN();
   DBK_MARK(tid == 0, 0);
   const int a_bytes = a.rows * 128;            // A rows of one k-block
   const int w_bytes = kBN * 128;               // 32 KB weight tile of one k-block

@@ -360,6 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
   const int nrows = row1 - row0;
   const int nmt = (nrows + RPT - 1) / RPT;
   const int total = nmt * a.nchunks;
+  DBK_TRACE_BEGIN();
   DBK_MARK(tid == 0, 0);
 
   if (tid == 0) {

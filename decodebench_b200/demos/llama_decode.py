@@ -195,7 +195,7 @@ def _build_layer(dim: int, batch: int, gen):
 
     @seq.stage
     def v_new(qkv):
-        return qkv[:, (H + Hkv) * D:].reshape(-1, Hkv, D).contiguous()
+        return qkv[:, (H + Hkv) * D:].reshape(-1, Hkv, D).clone()
 
     @seq.stage
     def K_all(k_rot, Kc):

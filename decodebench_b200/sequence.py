@@ -258,6 +258,11 @@ class Sequence:
         torch.manual_seed(seed)
         reps = list(input_replicas) if input_replicas else [inputs]
         self._validate_replicas(reps)
+        # One untraced run first: libraries allocate their workspaces lazily on
+        # first use (cuBLAS, for a stage's F.linear or einsum), and the temporary-
+        # allocation check would otherwise count that one-time allocation as the
+        # stage's own temporaries.
+        self._replay_body(reps[0])
         traces = self.trace(reps[0])
         if fused is not None:
             self._check_fused_output(fused, reps[0], torch)
