@@ -466,18 +466,33 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
           }
           // S^T[16 tokens x 8 heads] = K Q^T: tokens are the M rows (no padding);
           // heads 0..G-1 are the N columns. Two accumulators halve the MMA chain.
+          // The K loads are issued back to back before the MMAs, and the V loads
+          // right after them (they do not depend on the softmax), so their
+          // shared-memory latencies overlap with each other and with the softmax.
           float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+          uint32_t va[8][4];
           {
+            uint32_t ka[8][4];
             const int tok = t0 + (lane & 7) + 8 * ((lane >> 3) & 1);
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
               const int chunk = 2 * kk + (lane >> 4);     // 16-byte chunk of the 256-byte row
               const int h = chunk >> 3, c = chunk & 7;
               const int line = kv_line(tok, h, a.box_shift);
-              uint32_t ka[4];
-              ldsm_x4(kst + line * 128 + ((c ^ (line & 7)) << 4), ka);
-              Mma<T>::run((kk & 1) ? sb : sa, ka[0], ka[1], ka[2], ka[3], qa[kk][0], qa[kk][1]);
+              ldsm_x4(kst + line * 128 + ((c ^ (line & 7)) << 4), ka[kk]);
             }
+            const int vtok = t0 + (lane & 7) + 8 * (lane >> 4);
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {        // 16-dim m-tiles of V^T
+              const int chunk = 2 * mt + ((lane >> 3) & 1);
+              const int h = chunk >> 3, c = chunk & 7;
+              const int line = kv_line(vtok, h, a.box_shift);
+              ldsm_x4_t(vst + line * 128 + ((c ^ (line & 7)) << 4), va[mt]);
+            }
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              Mma<T>::run((kk & 1) ? sb : sa, ka[kk][0], ka[kk][1], ka[kk][2], ka[kk][3],
+                          qa[kk][0], qa[kk][1]);
           }
           // fragment: sc[0..1] = tokens t0+g, heads 2q, 2q+1; sc[2..3] = tokens t0+g+8
           const int g = lane >> 2;
@@ -521,20 +536,21 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
           }
           // O^T[128 dims x 8 heads] += V^T[dims x 16 tokens] P^T[16 tokens x 8 heads]
           {
-            const int tok = t0 + (lane & 7) + 8 * (lane >> 4);
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt) {        // 16-dim m-tiles
-              const int chunk = 2 * mt + ((lane >> 3) & 1);
-              const int h = chunk >> 3, c = chunk & 7;
-              const int line = kv_line(tok, h, a.box_shift);
-              uint32_t va[4];
-              ldsm_x4_t(vst + line * 128 + ((c ^ (line & 7)) << 4), va);
               float* d = &o[4 * mt];
               float acc4[4] = {d[0], d[1], d[2], d[3]};
-              Mma<T>::run(acc4, va[0], va[1], va[2], va[3], ph0, ph1);
-              if constexpr (std::is_same<T, __nv_bfloat16>::value)
-                Mma<T>::run(acc4, va[0], va[1], va[2], va[3], pl0, pl1);
+              Mma<T>::run(acc4, va[mt][0], va[mt][1], va[mt][2], va[mt][3], ph0, ph1);
               d[0] = acc4[0]; d[1] = acc4[1]; d[2] = acc4[2]; d[3] = acc4[3];
+            }
+            if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+#pragma unroll
+              for (int mt = 0; mt < 8; ++mt) {
+                float* d = &o[4 * mt];
+                float acc4[4] = {d[0], d[1], d[2], d[3]};
+                Mma<T>::run(acc4, va[mt][0], va[mt][1], va[mt][2], va[mt][3], pl0, pl1);
+                d[0] = acc4[0]; d[1] = acc4[1]; d[2] = acc4[2]; d[3] = acc4[3];
+              }
             }
           }
         }

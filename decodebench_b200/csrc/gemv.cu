@@ -468,7 +468,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
                                : xs_hi + (size_t)(b_ok ? bn : 0) * a.d_in) + kq;
   const uint16_t* xl = xs_lo + (size_t)(b_ok && bn < a.batch ? bn : 0) * a.d_in + kq;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-
+  float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+  // d_in <= 2 * KC with one B operand per k-step (no separate low-part MMA): a
+  // warp always multiplies the same 16 k-steps of each chunk, so its activation
+  // fragments are loaded from shared memory once instead of once per m-tile.
+  // (Not for the QKV epilogue, whose registers would then spill.)
+  const bool cache_b = MODE != MODE_QKV && !W8 && a.nchunks <= 2 && !(SPLIT && !packed);
+  uint32_t bfrag[2][16][2];
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      const int col = c * KC + warp * 256 + kk * 16;
+      const bool ok = cache_b && b_ok && c < a.nchunks && col < a.d_in;
+      bfrag[c][kk][0] = ok ? *reinterpret_cast<const uint32_t*>(xh + col) : 0u;
+      bfrag[c][kk][1] = ok ? *reinterpret_cast<const uint32_t*>(xh + col + 8) : 0u;
+    }
   for (int j = 0; j < total; ++j) {
     const int s = j % a.nstages;
     const int mt = j / a.nchunks, c = j - mt * a.nchunks;
@@ -505,26 +520,51 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
           }
         }
       }
-    } else
-#pragma unroll 4
-    for (int kk = 0; kk < 16; ++kk) {
-      const int k = warp * 256 + kk * 16;
-      if (k < seg) {
-        uint32_t af[4];
-        ldsm_x4(stage + k * 2, af);
-        uint32_t b0 = 0u, b1 = 0u;
-        if (b_ok) {
-          b0 = *reinterpret_cast<const uint32_t*>(xh + col0 + k);
-          b1 = *reinterpret_cast<const uint32_t*>(xh + col0 + k + 8);
-        }
-        Mma<T>::run(acc, af[0], af[1], af[2], af[3], b0, b1);
-        if (SPLIT && !packed) {
-          uint32_t l0 = 0u, l1 = 0u;
-          if (b_ok) {
-            l0 = *reinterpret_cast<const uint32_t*>(xl + col0 + k);
-            l1 = *reinterpret_cast<const uint32_t*>(xl + col0 + k + 8);
+    } else if (cache_b) {
+      // The activation fragments of this warp's k-steps were loaded once (before
+      // the loop); the weight loads of 8 k-steps are issued back to back before
+      // their MMAs, which alternate between two accumulator chains.
+      auto run_stage = [&](const uint32_t (&bb)[16][2]) {
+#pragma unroll
+        for (int k8 = 0; k8 < 16; k8 += 8) {
+          uint32_t af[8][4];
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const int k = warp * 256 + (k8 + kk) * 16;
+            if (k < seg) ldsm_x4(stage + k * 2, af[kk]);
           }
-          Mma<T>::run(acc, af[0], af[1], af[2], af[3], l0, l1);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const int k = warp * 256 + (k8 + kk) * 16;
+            if (k < seg)
+              Mma<T>::run((kk & 1) ? acc2 : acc, af[kk][0], af[kk][1], af[kk][2], af[kk][3],
+                          bb[k8 + kk][0], bb[k8 + kk][1]);
+          }
+        }
+      };
+      if (c == 0) run_stage(bfrag[0]);
+      else run_stage(bfrag[1]);
+    } else {
+#pragma unroll 4
+      for (int kk = 0; kk < 16; ++kk) {
+        const int k = warp * 256 + kk * 16;
+        if (k < seg) {
+          uint32_t af[4];
+          ldsm_x4(stage + k * 2, af);
+          uint32_t b0 = 0u, b1 = 0u;
+          if (b_ok) {
+            b0 = *reinterpret_cast<const uint32_t*>(xh + col0 + k);
+            b1 = *reinterpret_cast<const uint32_t*>(xh + col0 + k + 8);
+          }
+          Mma<T>::run(acc, af[0], af[1], af[2], af[3], b0, b1);
+          if (SPLIT && !packed) {
+            uint32_t l0 = 0u, l1 = 0u;
+            if (b_ok) {
+              l0 = *reinterpret_cast<const uint32_t*>(xl + col0 + k);
+              l1 = *reinterpret_cast<const uint32_t*>(xl + col0 + k + 8);
+            }
+            Mma<T>::run(acc, af[0], af[1], af[2], af[3], l0, l1);
+          }
         }
       }
     }
@@ -532,6 +572,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
     if (lane == 0) mbar_arrive(&empty[s]);
     if (c == a.nchunks - 1) {
       // m-tile done: accumulator rows (lane>>2) and (lane>>2)+8, columns 2*(lane&3) + {0,1}
+#pragma unroll
+      for (int e = 0; e < 4; ++e) { acc[e] += acc2[e]; acc2[e] = 0.f; }
       const int r = mt * 16 + (lane >> 2), n0 = 2 * (lane & 3);
       float* pw = part + (size_t)warp * nmt_max * 16 * pc;
       if (n0 < pc) {
