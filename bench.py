@@ -244,6 +244,12 @@ class F2(Workload):
         if self.world > 1 and not self.fused():
             self.gather_rows(self.h_local, self.h_full)
 
+    def torch_kernel(self, rep):
+        """Library baseline: the same step with PyTorch ops (cuBLAS GEMVs)."""
+        F = self.t.nn.functional
+        Wg, Wu = self.W[rep % self.nrep]
+        return F.silu(F.linear(self.x, Wg)) * F.linear(self.x, Wu)
+
     def e2e_setup(self):
         t = self.t
         self.x_host = self.x_cpu.pin_memory()
@@ -329,6 +335,13 @@ class F1(F2):
 
     def launch_bytes(self):
         return self.costs.rmsnorm_gemv_bytes(1, self.d_in, self.rows)
+
+    def torch_kernel(self, rep):
+        """Library baseline: RMSNorm as PyTorch elementwise ops, then F.linear (cuBLAS)."""
+        t = self.t
+        xf = self.x.float()
+        xn = (xf * t.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).half() * self.gamma
+        return t.nn.functional.linear(xn, self.W[rep % self.nrep])
 
     def run_kernel(self, rep):
         W = self.W[rep % self.nrep]
@@ -417,6 +430,12 @@ class F4(Workload):
     def run_kernel(self, rep):
         K, V = self.KV[rep % self.nrep]
         self.ops.flashdecode(self.q, K, V, out=self.o)
+
+    def torch_kernel(self, rep):
+        """Library baseline: torch scaled_dot_product_attention (its fused backends)."""
+        K, V = self.KV[rep % self.nrep]
+        q = self.q.unsqueeze(2)                      # [batch, H, 1, 128]
+        return self.t.nn.functional.scaled_dot_product_attention(q, K, V)
 
     def exchange(self):
         if self.world > 1:
@@ -623,6 +642,13 @@ class MLP(Workload):
     def run_kernel(self, rep):
         self.ops.gateup_swiglu(self.x, self.Wg, self.Wu, gamma=self.gamma, eps=1e-5, out=self.h)
         self.ops.gemv(self._gather_h(), self.Wd, out=self.y)
+
+    def torch_kernel(self, rep):
+        """Library baseline: RMSNorm, gate/up, SwiGLU and down with PyTorch ops (cuBLAS)."""
+        t, F = self.t, self.t.nn.functional
+        xf = self.x.float()
+        xn = (xf * t.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)).bfloat16() * self.gamma
+        return F.linear(F.silu(F.linear(xn, self.Wg)) * F.linear(xn, self.Wu), self.Wd)
 
     def exchange(self):
         if self.world > 1:
@@ -1075,7 +1101,10 @@ def main() -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "torch"], default="ours",
+                    help="ours: this build's kernels; reference: the reference's CPU "
+                         "implementation; torch: the same step with PyTorch / cuBLAS ops "
+                         "(a library baseline, one GPU)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="f2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=0,
@@ -1119,6 +1148,9 @@ def main() -> int:
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return 0
+
+    if args.impl == "torch":
+        return torch_arm(args, torch, world, rank)
 
     if world > 1:
         torch.cuda.set_device(local)
@@ -1247,6 +1279,48 @@ def main() -> int:
         sys.stdout.flush()
         sys.stderr.flush()
         os._exit(0)
+    return 0
+
+
+def torch_arm(args, torch, world, rank) -> int:
+    """The workload's step computed with PyTorch library ops (cuBLAS GEMV, SDPA) on
+    the same replicas, replayed from one CUDA graph of K steps: the library
+    baseline printed beside this build's numbers."""
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"impl": "torch", "unavailable": "the library arm runs on one GPU"}))
+        return 0
+    torch.cuda.set_device(0)
+    sys.path.insert(0, str(ROOT))
+    if args.rows and args.workload == "f2":
+        wl = F2(0, 1, torch, d_ff=args.rows)
+    elif args.rows and args.workload == "f1":
+        wl = F1(0, 1, torch, d_out=args.rows)
+    else:
+        wl = WORKLOADS[args.workload](0, 1, torch)
+    if not hasattr(wl, "torch_kernel"):
+        print(json.dumps({"impl": "torch", "unavailable":
+                          f"no PyTorch library path for workload {args.workload}"}))
+        return 0
+    s_cap = torch.cuda.Stream()
+    s_cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s_cap):
+        for r in range(wl.nrep):
+            wl.torch_kernel(r)
+    torch.cuda.current_stream().wait_stream(s_cap)
+    graphs = {}
+    for n in {args.warmup, args.steps}:
+        graphs[n] = _capture(torch, lambda n=n: [wl.torch_kernel(r % wl.nrep) for r in range(n)])
+    graphs[args.warmup].replay()
+    ms = timed(torch, lambda n: graphs[n].replay(), args.steps, 0)
+    us = ms * 1e3 / args.steps
+    peak, _ = peaks()
+    gbs = wl.step_bytes_total() / (us * 1e-6) / 1e9
+    print(json.dumps({"metric": METRIC, "impl": "torch", "value": round(gbs, 1), "unit": "GB/s",
+                      "us_per_step": round(us, 3), "frac_of_hbm_peak": round(gbs / peak, 4),
+                      "steps": args.steps, "warmup": args.warmup, "config": wl.describe(),
+                      "path": "torch ops on the same replicas (F.linear -> cuBLAS GEMV; "
+                              "scaled_dot_product_attention), one CUDA graph of K steps"}))
     return 0
 
 
