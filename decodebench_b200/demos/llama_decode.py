@@ -197,13 +197,19 @@ def _build_layer(dim: int, batch: int, gen):
     def v_new(qkv):
         return qkv[:, (H + Hkv) * D:].reshape(-1, Hkv, D).clone()
 
+    def _append(cache, new):                       # [B, Hkv, L+1, D], no temporaries
+        out = torch.empty(cache.shape[0], Hkv, L + 1, D, dtype=cache.dtype, device=cache.device)
+        out[:, :, :L].copy_(cache[:, :, :L])
+        out[:, :, L].copy_(new)
+        return out
+
     @seq.stage
     def K_all(k_rot, Kc):
-        return torch.cat([Kc[:, :, :L], k_rot[:, :, None]], dim=2)      # [B, Hkv, L+1, D]
+        return _append(Kc, k_rot)
 
     @seq.stage
     def V_all(v_new, Vc):
-        return torch.cat([Vc[:, :, :L], v_new[:, :, None]], dim=2)
+        return _append(Vc, v_new)
 
     @seq.stage
     def scores(q_rot, K_all):

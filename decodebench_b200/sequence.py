@@ -33,6 +33,15 @@ FUSED_REL_TOL = 2e-2
 _TEMP_WARN_MB = 0.1
 
 
+def _alloc_counter(torch) -> int:
+    """Bytes the stage's tensors asked the caching allocator for, cumulatively.
+    Requested bytes, not the rounded block sizes the allocator hands out: a
+    block rounded up (or left unsplit) for a stage's own output is not a
+    temporary of the stage."""
+    st = torch.cuda.memory_stats()
+    return st.get("requested_bytes.all.allocated", st["allocated_bytes.all.allocated"])
+
+
 @dataclass
 class _Stage:
     fn: Callable[..., Any]
@@ -163,12 +172,11 @@ class Sequence:
                         f"stage '{st.name}' tensor argument {j} is non-contiguous (shape="
                         f"{tuple(a.shape)}, stride={a.stride()}); materialize it "
                         "explicitly as a declared stage")
-            before = (torch.cuda.memory_stats()["allocated_bytes.all.allocated"]
-                      if watch_alloc else None)
+            before = _alloc_counter(torch) if watch_alloc else None
             out = st.fn(*args)
             self._check_stage_io(st, args, out, torch)
             if before is not None:
-                after = torch.cuda.memory_stats()["allocated_bytes.all.allocated"]
+                after = _alloc_counter(torch)
                 extra_mb = (after - before - out.nbytes) / 2**20
                 if extra_mb > _TEMP_WARN_MB:
                     warnings.warn(
