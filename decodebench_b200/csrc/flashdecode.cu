@@ -230,8 +230,11 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.nstages * kStage);
   uint64_t* empty = full + a.nstages;
-  float* mrg = reinterpret_cast<float*>(empty + a.nstages);              // [kWarps][G][kMrg]
-  int* tile0 = reinterpret_cast<int*>(mrg + kWarps * G * kMrg);           // [batch + 1]
+  // Segment-end combine buffer: one slot per warp on the CUDA-core path; on the
+  // tensor-core path warps 4-7 first fold their state into warps 0-3, so 4 slots.
+  constexpr int kMrgSlots = kMma ? kWarps / 2 : kWarps;
+  float* mrg = reinterpret_cast<float*>(empty + a.nstages);              // [kMrgSlots][G][kMrg]
+  int* tile0 = reinterpret_cast<int*>(mrg + kMrgSlots * G * kMrg);        // [batch + 1]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   DBK_TRACE_BEGIN();
@@ -637,21 +640,57 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
     // ---- segment done: merge the 8 warps' states in shared memory
     named_bar_sync(1, kConsumers);     // readers of the previous segment's mrg are done
     if constexpr (kMma) {
+      // Round 1: warps 4-7 store their (o, m, l); warps 0-3 fold their partner's state
+      // (warp w + 4, same fragment layout) into their own and store the result.
       const int g8 = lane >> 2, qd = lane & 3;
+      float lsum[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        float lsum = l[e];
+        lsum[e] = l[e];
 #pragma unroll
-        for (int o2 = 4; o2 < 32; o2 <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o2);
-        const int head = 2 * qd + e;
-        if (head < G) {
-          float* dst = mrg + (warp * G + head) * kMrg;
+        for (int o2 = 4; o2 < 32; o2 <<= 1) lsum[e] += __shfl_xor_sync(0xffffffffu, lsum[e], o2);
+      }
+      if (warp >= kWarps / 2) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int head = 2 * qd + e;
+          if (head < G) {
+            float* dst = mrg + ((warp - kWarps / 2) * G + head) * kMrg;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+              dst[16 * mt + g8] = o[4 * mt + e];
+              dst[16 * mt + g8 + 8] = o[4 * mt + 2 + e];
+            }
+            if (g8 == 0) { dst[kD] = m[e]; dst[kD + 1] = lsum[e]; }
+          }
+        }
+      }
+      named_bar_sync(1, kConsumers);
+      if (warp < kWarps / 2) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int head = 2 * qd + e;
+          float* dst = mrg + (warp * G + (head < G ? head : 0)) * kMrg;
+          const float mp = dst[kD], lp = dst[kD + 1];
+          const float M = fmaxf(m[e], mp);
+          const float fa = (lsum[e] > 0.f) ? exp2f(m[e] - M) : 0.f;
+          const float fb = (lp > 0.f) ? exp2f(mp - M) : 0.f;
+          float ov[16];
 #pragma unroll
           for (int mt = 0; mt < 8; ++mt) {
-            dst[16 * mt + g8] = o[4 * mt + e];
-            dst[16 * mt + g8 + 8] = o[4 * mt + 2 + e];
+            ov[2 * mt] = fmaf(fa, o[4 * mt + e], fb * dst[16 * mt + g8]);
+            ov[2 * mt + 1] = fmaf(fa, o[4 * mt + 2 + e], fb * dst[16 * mt + g8 + 8]);
           }
-          if (g8 == 0) { dst[kD] = m[e]; dst[kD + 1] = lsum; }
+          __syncwarp();                  // every lane has read the partner's m, l and o
+          if (head < G) {
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+              dst[16 * mt + g8] = ov[2 * mt];
+              dst[16 * mt + g8 + 8] = ov[2 * mt + 1];
+            }
+            if (g8 == 0) { dst[kD] = M; dst[kD + 1] = fmaf(fa, lsum[e], fb * lp); }
+          }
+          __syncwarp();
         }
       }
     } else {
@@ -671,10 +710,10 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
       const int g = idx / kD, d = idx - g * kD;
       float M = -INFINITY;
 #pragma unroll
-      for (int ww = 0; ww < kWarps; ++ww) M = fmaxf(M, mrg[(ww * G + g) * kMrg + kD]);
+      for (int ww = 0; ww < kMrgSlots; ++ww) M = fmaxf(M, mrg[(ww * G + g) * kMrg + kD]);
       float L = 0.f, O = 0.f;
 #pragma unroll
-      for (int ww = 0; ww < kWarps; ++ww) {
+      for (int ww = 0; ww < kMrgSlots; ++ww) {
         const float* src = mrg + (ww * G + g) * kMrg;
         const float f = (src[kD + 1] > 0.f) ? exp2f(src[kD] - M) : 0.f;
         L = fmaf(f, src[kD + 1], L);
@@ -723,7 +762,8 @@ size_t ws_bytes_for(int grid, int batch, int hq, int hkv) {
 template <typename T, int G>
 int launch_g(FdArgs a, cudaStream_t st, const DeviceInfo& dev, int grid, bool mma) {
   constexpr int kStage = 2 * kTile * kD * (int)sizeof(T);
-  const size_t fixed = 1024 + (size_t)kWarps * G * kMrg * 4 + (size_t)(a.batch + 1) * 4 + 64;
+  const size_t fixed = 1024 + (size_t)(mma ? kWarps / 2 : kWarps) * G * kMrg * 4 +
+                       (size_t)(a.batch + 1) * 4 + 64;
   static const int max_st = [] {   // DBK_FD_STAGES caps the ring depth (tuning knob)
     const char* v = std::getenv("DBK_FD_STAGES");
     const int n = v ? std::atoi(v) : kMaxStages;
