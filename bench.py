@@ -1024,14 +1024,36 @@ class StepGraphs:
             self.graphs[n].replay()
 
 
-def timed(torch, run, steps: int, warmup: int) -> float:
+_FLUSH = {}
+
+
+def l2_flush(torch) -> None:
+    """Overwrite a 256 MB buffer (twice the 126 MB L2) on the current device."""
+    dev = torch.cuda.current_device()
+    buf = _FLUSH.get(dev)
+    if buf is None:
+        buf = _FLUSH[dev] = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    buf.zero_()
+
+
+def timed(torch, run, steps: int, warmup: int, host_latency: bool = True) -> float:
     """Device ms for run(steps) after run(warmup); barrier + sync on both sides,
-    CUDA events on the current stream, max over ranks."""
+    CUDA events on the current stream, max over ranks.
+
+    With host_latency=False, L2 is flushed (the warm-up's last replicas would
+    otherwise still be cached for the first timed steps) and a short device-side
+    delay is queued ahead of the start event, so the work that run() submits is
+    already queued when the start event fires: the region times the steps on the
+    device, not the host's submission of a graph (several us per replay, which
+    would otherwise weigh on short runs)."""
     if warmup:
         run(warmup)
     barrier_sync(torch)
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
+    if not host_latency:
+        l2_flush(torch)
+        torch.cuda._sleep(DELAY_CYCLES)
     a.record()
     run(steps)
     b.record()
@@ -1090,6 +1112,9 @@ def cpu_baseline(wl, threads: int, budget_s: float, steps=None, warmup=1) -> dic
                        "weights pre-converted fp16->fp32 once, untimed; median step time, "
                        "GB/s over the same algorithmic fp16 bytes")}
 
+
+# Device-side delay (GPU clock cycles, ~100 us) queued ahead of a device-timed region.
+DELAY_CYCLES = 200_000
 
 # Seconds of CPU work per cpu_baseline measurement (both arms).
 CPU_BUDGET_S = 12.0
@@ -1182,7 +1207,7 @@ def main() -> int:
     graphs.run(args.warmup)
     barrier_sync(torch)
     t_begin = time.perf_counter()
-    ms = timed(torch, graphs.run, args.steps, 0)
+    ms = timed(torch, graphs.run, args.steps, 0, host_latency=False)
     t_end = time.perf_counter()
     # Keep identical steps running until the sampler has seen >= 5 samples, so
     # that a short timed region still has a clock record around it.
@@ -1205,7 +1230,7 @@ def main() -> int:
     if world > 1:
         kgraphs = StepGraphs(torch, wl, with_exchange=False)
         kgraphs.prepare(args.warmup, args.steps)
-        kms = timed(torch, kgraphs.run, args.steps, args.warmup)
+        kms = timed(torch, kgraphs.run, args.steps, args.warmup, host_latency=False)
     else:
         kms = ms
     k_us = kms * 1e3 / args.steps
@@ -1242,7 +1267,7 @@ def main() -> int:
         egraphs[n] = _capture(torch, lambda n=n: [wl.e2e_step() for _ in range(n)])
     torch.cuda.synchronize()
     egraphs[args.warmup].replay()
-    e_ms = timed(torch, lambda n: egraphs[n].replay(), args.steps, 0)
+    e_ms = timed(torch, lambda n: egraphs[n].replay(), args.steps, 0, host_latency=False)
     e_us = e_ms * 1e3 / args.steps
     e2e = {"value": round(wl.step_bytes_total() / (e_us * 1e-6) / 1e9, 1), "unit": "GB/s",
            "us_per_step": round(e_us, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -1267,6 +1292,11 @@ def main() -> int:
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "fp16", "data": "synthetic, seeded (torch.Generator)",
                 "config": wl.describe(), "roofline": roofline, "cpu_baseline": cb, "e2e": e2e,
+                "timing": ("one CUDA graph of exactly the K timed steps, replayed once between "
+                           "two CUDA events on the launching stream; L2 is flushed (256 MB write) "
+                           "and a ~100 us device-side delay is queued first, so the timed steps "
+                           "start from a cold L2 with the graph already queued (host submission "
+                           "latency excluded); weights rotate over replicas > 2x L2; max over ranks"),
                 "clocks": clocks, "gpu_launches": args.steps * (wl.kernels_per_step + (
                     wl.exchanges_per_step if world > 1 and wl.comm is not None else 0))}
         print(json.dumps(line))
@@ -1312,7 +1342,7 @@ def torch_arm(args, torch, world, rank) -> int:
     for n in {args.warmup, args.steps}:
         graphs[n] = _capture(torch, lambda n=n: [wl.torch_kernel(r % wl.nrep) for r in range(n)])
     graphs[args.warmup].replay()
-    ms = timed(torch, lambda n: graphs[n].replay(), args.steps, 0)
+    ms = timed(torch, lambda n: graphs[n].replay(), args.steps, 0, host_latency=False)
     us = ms * 1e3 / args.steps
     peak, _ = peaks()
     gbs = wl.step_bytes_total() / (us * 1e-6) / 1e9
