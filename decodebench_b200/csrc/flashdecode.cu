@@ -177,28 +177,34 @@ __device__ __forceinline__ bool wait_count(const int* p, int v) {
 
 // Log-sum-exp merge of row (b, hk)'s partials (reference f4_reduce_kernel,
 // validation/src/kernels/fused/f4.cu:294-319), by the consumer threads of the
-// CTA that holds the row's last tile, once the others have arrived: M = max_c m_c, out = sum_c 2^(m_c - M) o_c /
-// sum_c 2^(m_c - M) l_c (m in log2 units), contributors in CTA order (results do
-// not depend on timing). Every thread loads up to 8 contributors' (m, l, o) at
-// once and rescales its running sums per batch of 8, so a merge costs about one
-// L2 round trip per 8 contributors.
+// CTA that holds the row's last tile, once the others have arrived:
+// M = max_c m_c, out = sum_c 2^(m_c - M) o_c / sum_c 2^(m_c - M) l_c (m in log2
+// units), contributors in CTA order (results do not depend on timing). The
+// contributors' workspace slots are worked out once into shared memory (`slots`,
+// np ints); then every thread issues all of its loads -- (m, l) and o of every
+// contributor for its outputs -- before using any of them, so a merge costs
+// about one L2 round trip whatever the number of contributors.
 template <typename T, int G>
 __device__ void merge_row(const FdArgs& a, int b, int hk, int rs, int ntb, int64_t Ttot,
-                          int grid, int tid) {
+                          int grid, int tid, int* slots) {
   T* out = static_cast<T*>(a.out);
   const int c_first = owner(rs, Ttot, grid), c_last = owner(rs + ntb - 1, Ttot, grid);
   const int np = c_last - c_first + 1;
+  for (int i = tid; i < np; i += kConsumers) {
+    const int c = c_first + i;
+    slots[i] = 2 * c + (range_start(c, Ttot, grid) >= rs ? 0 : 1);
+  }
+  named_bar_sync(1, kConsumers);
   for (int idx = tid; idx < G * kD; idx += kConsumers) {
     const int g = idx / kD, d = idx - g * kD;
     float M = -INFINITY, L = 0.f, O = 0.f;
-    for (int c0 = 0; c0 < np; c0 += 8) {
-      float mc[8], lc[8], oc[8];
+    for (int c0 = 0; c0 < np; c0 += 16) {
+      float mc[16], lc[16], oc[16];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < 16; ++k) {
         mc[k] = -INFINITY; lc[k] = 0.f; oc[k] = 0.f;
         if (c0 + k < np) {
-          const int c = c_first + c0 + k;
-          const int sl = 2 * c + (range_start(c, Ttot, grid) >= rs ? 0 : 1);
+          const int sl = slots[c0 + k];
           const float2 ml = __ldcg(&a.part_ml[(size_t)sl * G + g]);
           mc[k] = ml.x; lc[k] = ml.y;
           oc[k] = __ldcg(&a.part_o[((size_t)sl * G + g) * kD + d]);
@@ -206,12 +212,12 @@ __device__ void merge_row(const FdArgs& a, int b, int hk, int rs, int ntb, int64
       }
       float Mn = M;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) Mn = fmaxf(Mn, mc[k]);
+      for (int k = 0; k < 16; ++k) Mn = fmaxf(Mn, mc[k]);
       const float sc = (M == -INFINITY) ? 0.f : exp2f(M - Mn);
       L *= sc;
       O *= sc;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < 16; ++k) {
         const float f = (lc[k] > 0.f) ? exp2f(mc[k] - Mn) : 0.f;
         L = fmaf(f, lc[k], L);
         O = fmaf(f, oc[k], O);
@@ -219,6 +225,93 @@ __device__ void merge_row(const FdArgs& a, int b, int hk, int rs, int ntb, int64
       M = Mn;
     }
     out[((size_t)b * a.hq + (size_t)hk * G + g) * kD + d] = Elem<T>::from_f(O / L);
+  }
+}
+
+// The same merge with the row's partials first staged in shared memory: the
+// consumer threads copy every contributor's (m, l) and o into `buf` (the ring,
+// idle once the CTA's tiles are consumed) with independent 16-byte loads -- about
+// one L2 round trip for the whole row -- then the weights and sums come from
+// shared memory. `buf` must hold np * G * (kD + 2) floats (merge_staged_fits).
+__host__ __device__ inline bool merge_staged_fits(int np, int G, size_t buf_bytes) {
+  return (size_t)np * G * (kD + 2) * sizeof(float) + (size_t)G * sizeof(float) <= buf_bytes;
+}
+
+template <typename T, int G>
+__device__ void merge_row_staged(const FdArgs& a, int b, int hk, int rs, int ntb, int64_t Ttot,
+                                 int grid, int tid, int* slots, float* buf) {
+  T* out = static_cast<T*>(a.out);
+  const int c_first = owner(rs, Ttot, grid), c_last = owner(rs + ntb - 1, Ttot, grid);
+  const int np = c_last - c_first + 1;
+  float* o_s = buf;                                   // [np][G][kD]
+  float* w_s = o_s + (size_t)np * G * kD;             // [np][G]: m, then the weight
+  float* l_s = w_s + np * G;                          // [np][G]
+  float* inv_l = l_s + np * G;                        // [G]
+  for (int i = tid; i < np; i += kConsumers) {
+    const int c = c_first + i;
+    slots[i] = 2 * c + (range_start(c, Ttot, grid) >= rs ? 0 : 1);
+  }
+  named_bar_sync(1, kConsumers);
+  constexpr int kV = G * kD / 4;                      // float4 per contributor
+  const int nv = np * kV, nml = np * G;
+  // Every (m, l) pair and every float4 of o in flight at once: the loads of up to
+  // 16 float4 per thread go to registers before any shared-memory store (a store
+  // through the generic pointer could alias a later load, so loads and stores
+  // interleaved would run one round trip each).
+  float2 ml0 = make_float2(0.f, 0.f);
+  if (tid < nml) ml0 = __ldcg(&a.part_ml[(size_t)slots[tid / G] * G + (tid % G)]);
+  for (int base = tid; base < nv; base += 16 * kConsumers) {
+    float4 r[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int v = base + k * kConsumers;
+      if (v < nv) {
+        const int c = v / kV, rr = v - c * kV;
+        r[k] = __ldcg(reinterpret_cast<const float4*>(a.part_o + (size_t)slots[c] * G * kD) + rr);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int v = base + k * kConsumers;
+      if (v < nv) reinterpret_cast<float4*>(o_s)[v] = r[k];
+    }
+  }
+  if (tid < nml) {
+    w_s[tid] = ml0.x;
+    l_s[tid] = ml0.y;
+  }
+  for (int i = kConsumers + tid; i < nml; i += kConsumers) {
+    const float2 ml = __ldcg(&a.part_ml[(size_t)slots[i / G] * G + (i % G)]);
+    w_s[i] = ml.x;
+    l_s[i] = ml.y;
+  }
+  named_bar_sync(1, kConsumers);
+  DBK_MARK(tid == 0, 13);
+  // Weights: warp g handles head g, its lanes the contributors.
+  {
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int g = warp; g < G; g += kConsumers / 32) {
+      float M = -INFINITY;
+      for (int c = lane; c < np; c += 32) M = fmaxf(M, w_s[c * G + g]);
+      M = warp_max(M);
+      float L = 0.f;
+      for (int c = lane; c < np; c += 32) {
+        const float lc = l_s[c * G + g];
+        const float f = (lc > 0.f) ? exp2f(w_s[c * G + g] - M) : 0.f;
+        w_s[c * G + g] = f;
+        L = fmaf(f, lc, L);
+      }
+      L = warp_sum(L);
+      if (lane == 0) inv_l[g] = 1.f / L;
+    }
+  }
+  named_bar_sync(1, kConsumers);
+  DBK_MARK(tid == 0, 14);
+  for (int idx = tid; idx < G * kD; idx += kConsumers) {
+    const int g = idx / kD;
+    float O = 0.f;
+    for (int c = 0; c < np; ++c) O = fmaf(w_s[c * G + g], o_s[(size_t)c * G * kD + idx], O);
+    out[((size_t)b * a.hq + (size_t)hk * G) * kD + idx] = Elem<T>::from_f(O * inv_l[g]);
   }
 }
 
@@ -743,8 +836,18 @@ __global__ void __launch_bounds__(kThreads, 1) flashdecode_kernel(const __grid_c
     // resident together (one per SM, grid <= SM count), so the wait ends.
     int* cnt = &a.done[pend_b * a.hkv + pend_hk];
     if (tid == 0) s_last = wait_count(cnt, pend_np - 1) ? 1 : 0;
+    DBK_MARK(tid == 0, 12);
     named_bar_sync(1, kConsumers);
-    if (s_last) merge_row<T, G>(a, pend_b, pend_hk, pend_rs, pend_ntb, Ttot, grid, tid);
+    // mrg and the ring are free once every consumer has passed the barrier above
+    // (every stage the producer filled has been consumed).
+    if (s_last) {
+      if (merge_staged_fits(pend_np, G, (size_t)a.nstages * kStage))
+        merge_row_staged<T, G>(a, pend_b, pend_hk, pend_rs, pend_ntb, Ttot, grid, tid,
+                               reinterpret_cast<int*>(mrg), reinterpret_cast<float*>(smem));
+      else
+        merge_row<T, G>(a, pend_b, pend_hk, pend_rs, pend_ntb, Ttot, grid, tid,
+                        reinterpret_cast<int*>(mrg));
+    }
     if (tid == 0) *cnt = 0;                   // ready for the next launch
     DBK_MARK(tid == 0, 7);
   }
@@ -834,7 +937,13 @@ extern "C" int dbk_flashdecode(const void* q, const void* k_cache, const void* v
   // Grid: one CTA per SM, or fewer when there are fewer tiles than SMs
   // (an upper bound on tiles: every sequence at max_len).
   const int64_t max_tiles = (int64_t)batch * n_kv_heads * ((max_len + kTile - 1) / kTile);
-  const int grid = (int)(max_tiles < dev.num_sms ? max_tiles : dev.num_sms);
+  static const int min_tiles = [] {   // DBK_FD_MIN_TILES: fewest tiles per CTA (experiments)
+    const char* v = std::getenv("DBK_FD_MIN_TILES");
+    const int n = v ? std::atoi(v) : 1;
+    return n < 1 ? 1 : n;
+  }();
+  const int64_t want = (max_tiles + min_tiles - 1) / min_tiles;
+  const int grid = (int)(want < dev.num_sms ? want : dev.num_sms);
   const size_t need = ws_bytes_for(dev.num_sms, batch, n_q_heads, n_kv_heads);
   if (!workspace || workspace_bytes < need) return DBK_EWORKSPACE;
   if (!aligned16(workspace)) return DBK_EALIGN;
