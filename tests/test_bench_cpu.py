@@ -49,3 +49,42 @@ def test_ops_refuse_cpu_tensors():
     kv = torch.zeros(1, 2, 64, 128, dtype=torch.float16)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.flashdecode(q, kv, kv)
+
+
+def _bench_module():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("dbk_bench", ROOT / "bench.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_step_graphs_cover_exactly_k_steps():
+    """The timed region replays graphs covering exactly K steps: one graph of K
+    steps up to the cap, then cap-sized graphs plus one remainder graph."""
+    bench = _bench_module()
+    sg = bench.StepGraphs.__new__(bench.StepGraphs)
+    sg.cap = 4096
+    for k in (1, 5, 20, 4096, 4097, 10000):
+        chunks = sg._chunks(k)
+        assert sum(chunks) == k
+        assert all(0 < c <= 4096 for c in chunks)
+        assert len(chunks) == (k + 4095) // 4096
+    assert sg._chunks(20) == [20]
+
+
+def test_cpu_sampler_runs_at_least_the_minimum_steps():
+    """Both CPU arms use the same time-budgeted sampler: warm-up, then at least
+    min_steps measured steps, however short the budget."""
+    bench = _bench_module()
+
+    class Fake:
+        calls = 0
+
+        def cpu_step(self, threads):
+            Fake.calls += 1
+
+    med, n = bench.cpu_time(Fake(), 1, budget_s=0.0, warmup=1, min_steps=10)
+    assert n == 10 and med >= 0.0
+    assert Fake.calls >= 11
