@@ -871,9 +871,9 @@ class QKV(Workload):
 class Layer(Workload):
     """One whole Llama decode layer for one new token (the scope's next rows, not a
     benchmark config): d 4096, 32 q / 8 kv heads, FFN 11008, fp16, contiguous cache
-    of 1024 tokens + the new one; five kernels chained with programmatic dependent
-    launch (QKV + RoPE + append, FlashDecode, o_proj + residual, RMSNorm + gate/up
-    + SwiGLU, down + residual). Single GPU: a sharded layer needs a reduction after
+    of 1024 tokens + the new one; four kernels chained with programmatic dependent
+    launch (QKV + RoPE + append, FlashDecode, o_proj + residual, and the persistent
+    MLP block: RMSNorm + gate/up + SwiGLU, grid barrier, down + residual). Single GPU: a sharded layer needs a reduction after
     o_proj and down, which this build does not provide."""
 
     name = "layer"
@@ -890,6 +890,11 @@ class Layer(Workload):
         _, self.inputs, self.reps, self.fused = build_demo("layer", dim=4096, batch=1)
         self.nrep = len(self.reps)
         self.out = None
+        from decodebench_b200 import ops
+
+        # the MLP block is one persistent launch unless DBK_MLP_BLOCK=0
+        self.fused(self.reps[0])
+        self.kernels_per_step = 4 if ops._MLP_BLOCK and not ops._mlp_block_refused else 5
 
     def describe(self):
         return {"workload": "whole Llama decode layer, d 4096, 32 q / 8 kv heads, FFN 11008, fp16, "

@@ -26,6 +26,7 @@ enum DeviceError : int {
   kDevTimeoutDrain = 4,     // waited too long for in-flight copies at exit
   kDevTimeoutPeer = 5,      // waited too long for another GPU's all-gather signal
   kDevTimeoutMerge = 6,     // waited too long for the other contributors of a tile
+  kDevTimeoutGrid = 7,      // waited too long at a grid-wide barrier of a persistent kernel
 };
 
 extern __device__ int dbk_device_error;
@@ -49,6 +50,11 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Adds 1 to *p with release semantics at GPU scope (prior writes visible first).
+__device__ __forceinline__ void arrive_release_gpu(int* p) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p) : "memory");
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -1010,3 +1010,381 @@ extern "C" int dbk_gateup_swiglu_fp8(const void* x, const void* gamma, const voi
   a.y = h; a.batch = batch; a.d_in = d_in; a.d_out = d_ff; a.eps = eps;
   return gemv_dispatch(MODE_SWIGLU, a, dtype, static_cast<cudaStream_t>(stream));
 }
+
+// ---------------------------------------------------------------------------
+// Persistent MLP block (batch 1..4): h = silu(Wg x') * (Wu x') with x' = x, or the
+// RMSNorm of x when gamma is given, then y = Wd h (+ residual), in ONE launch:
+//   * one CTA per SM with gemv_mma_kernel's producer / consumer split and ring;
+//     the producer walks the CTA's gate/up rows and then, without a pause, its
+//     down rows, so the ring already holds Wd when phase 2 may start;
+//   * phase 1 writes h to global memory, then every CTA meets the others at a
+//     grid-wide barrier (two counters in the workspace, bounded wait, left at
+//     zero by the last CTA through) -- the only synchronisation between the
+//     GEMVs, instead of a kernel boundary and a second pipeline fill;
+//   * phase 2 stages all of h (exact in 16 bits: no low part) over the shared
+//     bytes that phase 1 used for its activation stage and partial sums.
+// Per output the arithmetic is that of dbk_gateup_swiglu followed by dbk_gemv
+// (the same k-step order per warp, the same fixed warp order in the epilogue,
+// fp32 accumulation), so the two agree bit for bit.
+// Reference semantics: fused f2_kernel (validation/src/kernels/fused/f2.cu:17-76)
+// and the down projection of the decode MLP (src/decodebench/demos/llama_decode.py:77-87).
+namespace dbk {
+namespace {
+
+struct MlpArgs {
+  GemvArgs g;        // phase 1: MODE_SWIGLU, y = h
+  GemvArgs d;        // phase 2: MODE_PLAIN, x = h, with residual
+  int* sync;         // [2]: arrivals, departures (zero before and after a launch)
+  int nstages;
+  int region_bytes;  // shared bytes after the ring shared by the two phases
+};
+
+// CTA rows [row0, row1) of a d_out-row operand over G CTAs.
+__device__ __forceinline__ int2 cta_rows(int d_out, int G) {
+  return make_int2((int)(((int64_t)blockIdx.x * d_out) / G),
+                   (int)(((int64_t)(blockIdx.x + 1) * d_out) / G));
+}
+
+// Producer: one phase's (m-tile, K chunk) stages into the ring, continuing the
+// ring position j. NMAT = 2 puts the gate rows in slots 0..7 and the up rows in
+// slots 8..15 of a stage. False when a bounded wait gave up.
+template <int NMAT>
+__device__ __forceinline__ bool mlp_produce(const GemvArgs& a, int2 rows, uint8_t* ring,
+                                            uint64_t* full, uint64_t* empty, int nst, int& j,
+                                            uint64_t pol) {
+  constexpr int RPT = 16 / NMAT;
+  const int nmt = (rows.y - rows.x + RPT - 1) / RPT;
+  const uint8_t* W0 = static_cast<const uint8_t*>(a.w0);
+  const uint8_t* W1 = static_cast<const uint8_t*>(a.w1);
+  for (int t = 0; t < nmt * a.nchunks; ++t, ++j) {
+    const int s = j % nst;
+    if (j >= nst && !mbar_wait(&empty[s], ((j / nst) & 1) ^ 1, kDevTimeoutEmpty)) return false;
+    const int mt = t / a.nchunks, c = t - mt * a.nchunks;
+    const int col0 = c * kMmaKC;
+    const int seg = min(kMmaKC, a.d_in - col0);
+    const int r_first = rows.x + mt * RPT;
+    const int valid = min(RPT, rows.y - r_first);
+    mbar_arrive_expect_tx(&full[s], (uint32_t)(valid * NMAT * seg * 2));
+    uint8_t* dst = ring + (size_t)s * kMmaStage;
+    for (int q = 0; q < valid; ++q) {
+      const size_t off = ((size_t)(r_first + q) * a.d_in + col0) * 2;
+      bulk_g2s(dst + q * kMmaSlot, W0 + off, (uint32_t)(seg * 2), &full[s], pol);
+      if constexpr (NMAT == 2)
+        bulk_g2s(dst + (8 + q) * kMmaSlot, W1 + off, (uint32_t)(seg * 2), &full[s], pol);
+    }
+  }
+  return true;
+}
+
+// Grid-wide barrier, called by one thread per CTA after the CTA's stores.
+// Arrivals count up to the grid size; the CTA that departs last puts both
+// counters back to zero (no CTA reads them again in this launch).
+__device__ __forceinline__ bool grid_barrier(int* sync, int nblocks) {
+  __threadfence();
+  arrive_release_gpu(&sync[0]);
+  uint32_t n = 0;
+  const uint32_t lim = spin_limit();
+  bool ok = true;
+  while (ld_acquire_gpu(&sync[0]) < nblocks) {
+    if (++n >= lim) { record_error(kDevTimeoutGrid); ok = false; break; }
+    __nanosleep(32);
+  }
+  if (atomicAdd(&sync[1], 1) == nblocks - 1) {
+    sync[0] = 0;
+    sync[1] = 0;
+  }
+  return ok;
+}
+
+// Consumers: one phase's MMA loop over the ring, writing each m-tile's per-warp
+// partials to `part`. The activation fragments are read from shared memory per
+// k-step. TWO_CHAINS alternates the k-steps between two accumulators and adds
+// them at the end of the m-tile -- the order of gemv_mma_kernel's register-cached
+// variant (d_in <= 2 chunks); without it one chain, the order of its per-k-step
+// variant. With skip, stages are waited for and released without computing
+// (drains the ring after a failed barrier). False when a bounded wait gave up.
+template <typename T, int NMAT, bool TWO_CHAINS>
+__device__ __forceinline__ bool mlp_consume(const GemvArgs& a, int2 rows, const uint8_t* ring,
+                                            uint64_t* full, uint64_t* empty, int nst, int& j,
+                                            float* part, int pc, const uint16_t* xs, bool packed,
+                                            bool skip) {
+  constexpr int RPT = 16 / NMAT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nmt = (rows.y - rows.x + RPT - 1) / RPT;
+  const int a_row = (lane & 7) + 8 * ((lane >> 3) & 1);
+  const uint32_t a_lane_off = (uint32_t)(a_row * kMmaSlot + (8 * (lane >> 4)) * 2);
+  const int bn = lane >> 2;
+  const bool b_ok = bn < pc;
+  const int kq = 2 * (lane & 3);
+  // packed: columns [batch, 2 batch) hold the low parts of the activation
+  const uint16_t* xh = (packed && bn >= a.batch ? xs + (size_t)a.batch * a.d_in +
+                                                      (size_t)(bn - a.batch) * a.d_in
+                                                : xs + (size_t)(b_ok ? bn : 0) * a.d_in) + kq;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int t = 0; t < nmt * a.nchunks; ++t, ++j) {
+    const int s = j % nst;
+    const int mt = t / a.nchunks, c = t - mt * a.nchunks;
+    const int col0 = c * kMmaKC;
+    const int seg = min(kMmaKC, a.d_in - col0);
+    if (!mbar_wait(&full[s], (j / nst) & 1, kDevTimeoutFull)) return false;
+    const uint32_t stage = smem_u32(ring + (size_t)s * kMmaStage) + a_lane_off;
+    if (!skip) {
+#pragma unroll 4
+      for (int kk = 0; kk < 16; ++kk) {
+        const int k = warp * 256 + kk * 16;
+        if (k < seg) {
+          uint32_t af[4];
+          ldsm_x4(stage + k * 2, af);
+          uint32_t b0 = 0u, b1 = 0u;
+          if (b_ok) {
+            b0 = *reinterpret_cast<const uint32_t*>(xh + col0 + k);
+            b1 = *reinterpret_cast<const uint32_t*>(xh + col0 + k + 8);
+          }
+          Mma<T>::run((TWO_CHAINS && (kk & 1)) ? acc2 : acc, af[0], af[1], af[2], af[3], b0, b1);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (c == a.nchunks - 1 && !skip) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) { acc[e] += acc2[e]; acc2[e] = 0.f; }
+      const int r = mt * 16 + (lane >> 2), n0 = 2 * (lane & 3);
+      float* pw = part + (size_t)warp * nmt * 16 * pc;
+      if (n0 < pc) {
+        pw[(size_t)r * pc + n0] = acc[0];
+        pw[(size_t)(r + 8) * pc + n0] = acc[2];
+      }
+      if (n0 + 1 < pc) {
+        pw[(size_t)r * pc + n0 + 1] = acc[1];
+        pw[(size_t)(r + 8) * pc + n0 + 1] = acc[3];
+      }
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    }
+  }
+  return true;
+}
+
+// Sum of the 8 warp partials of CTA row r (slot within its m-tile), column b.
+__device__ __forceinline__ float mlp_row_sum(const float* part, int nmt, int pc, int mt, int slot,
+                                             int b, int batch, bool packed) {
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    const float* pr = part + ((size_t)w * nmt * 16 + mt * 16 + slot) * pc;
+    t += packed ? pr[b] + pr[batch + b] : pr[b];
+  }
+  return t;
+}
+
+template <typename T, bool SPLIT>
+__global__ void __launch_bounds__(kThreads, 1) mlp_block_kernel(const MlpArgs m) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const int nst = m.nstages;
+  uint8_t* ring = smem_raw;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)nst * kMmaStage);
+  uint64_t* empty = full + nst;
+  uint8_t* region = reinterpret_cast<uint8_t*>(empty + nst);
+  __shared__ float red[kConsumerWarps][8];
+  __shared__ float inv_rms[8];
+  __shared__ int s_ok;
+
+  const GemvArgs& A = m.g;
+  const GemvArgs& D = m.d;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x;
+  const int2 rows_a = cta_rows(A.d_out, G);
+
+  if (tid == 0) {
+    for (int s = 0; s < nst; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;");
+
+  if (warp == kConsumerWarps) {
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      int j = 0;
+      if (mlp_produce<2>(A, rows_a, ring, full, empty, nst, j, pol))
+        mlp_produce<1>(D, cta_rows(D.d_out, G), ring, full, empty, nst, j, pol);
+    }
+    return;
+  }
+
+  // -------------------------------------------------- phase 1: gate/up + SwiGLU
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int nmt_a = (rows_a.y - rows_a.x + 7) / 8;
+  const int pc_a = A.pcols;
+  const bool packed_a = SPLIT && pc_a > A.batch;
+  float* part = reinterpret_cast<float*>(region);
+  uint16_t* xs = reinterpret_cast<uint16_t*>(part + (size_t)kConsumerWarps * nmt_a * 16 * pc_a);
+  {
+    const T* x = static_cast<const T*>(A.x);
+    const T* gam = static_cast<const T*>(A.gamma);
+    uint16_t* xs_lo = xs + (size_t)A.batch * A.d_in;
+    float ss[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) ss[b] = 0.f;
+    const int per_row = A.d_in / 8;
+    for (int v = tid; v < A.batch * per_row; v += kConsumers) {
+      const int b = v / per_row, c = (v - b * per_row) * 8;
+      float f[8], g[8];
+      unpack8<T>(ldg_nc_v4(x + (size_t)b * A.d_in + c), f);
+      if (gam != nullptr) unpack8<T>(ldg_nc_v4(gam + c), g);
+      uint32_t hi[4], lo[4];
+      float sq = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        float p0 = f[e], p1 = f[e + 1];
+        sq = fmaf(p0, p0, fmaf(p1, p1, sq));
+        if (gam != nullptr) { p0 *= g[e]; p1 *= g[e + 1]; }
+        hi[e / 2] = Mma<T>::pack(p0, p1);
+        const float2 h = Elem<T>::unpack2(hi[e / 2]);
+        lo[e / 2] = Mma<T>::pack(p0 - h.x, p1 - h.y);
+      }
+#pragma unroll
+      for (int bb = 0; bb < 8; ++bb) ss[bb] += (bb == b) ? sq : 0.f;
+      *reinterpret_cast<uint4*>(xs + (size_t)b * A.d_in + c) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      if (SPLIT)
+        *reinterpret_cast<uint4*>(xs_lo + (size_t)b * A.d_in + c) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const float t = warp_sum(ss[b]);
+      if (lane == 0) red[warp][b] = t;
+    }
+  }
+  named_bar_sync(1, kConsumers);
+  if (tid < 8) {
+    float v = 1.f;
+    if (A.gamma != nullptr && tid < A.batch) {
+      float t = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w) t += red[w][tid];
+      v = rsqrtf(t / (float)A.d_in + A.eps);
+    }
+    inv_rms[tid] = v;
+  }
+  int j = 0;
+  if (!mlp_consume<T, 2, true>(A, rows_a, ring, full, empty, nst, j, part, pc_a, xs, packed_a,
+                               false))
+    return;
+  named_bar_sync(1, kConsumers);
+  {
+    T* h = static_cast<T*>(A.y);
+    const int nrows = rows_a.y - rows_a.x;
+    for (int idx = tid; idx < nrows * A.batch; idx += kConsumers) {
+      const int b = idx / nrows, r = idx - b * nrows;
+      const int mt = r / 8, q = r - mt * 8;
+      const float sc = inv_rms[b];
+      const float v = silu(mlp_row_sum(part, nmt_a, pc_a, mt, q, b, A.batch, packed_a) * sc) *
+                      (mlp_row_sum(part, nmt_a, pc_a, mt, 8 + q, b, A.batch, packed_a) * sc);
+      h[(size_t)b * A.d_out + rows_a.x + r] = Elem<T>::from_f(v);
+    }
+  }
+  named_bar_sync(1, kConsumers);      // every h store of this CTA precedes the barrier
+  if (tid == 0) s_ok = grid_barrier(m.sync, G) ? 1 : 0;
+  named_bar_sync(1, kConsumers);
+  const bool skip = s_ok == 0;
+
+  // -------------------------------------------------- phase 2: down (+ residual)
+  const int2 rows_d = cta_rows(D.d_out, G);
+  const int nmt_d = (rows_d.y - rows_d.x + 15) / 16;
+  const int pc_d = D.batch;
+  xs = reinterpret_cast<uint16_t*>(part + (size_t)kConsumerWarps * nmt_d * 16 * pc_d);
+  if (!skip) {
+    // h was written by this launch: read it through L2 (not the non-coherent path)
+    const uint4* src = static_cast<const uint4*>(D.x);
+    for (int v = tid; v < D.batch * D.d_in / 8; v += kConsumers)
+      reinterpret_cast<uint4*>(xs)[v] = __ldcg(src + v);
+  }
+  named_bar_sync(1, kConsumers);
+  // d_ff > 2 chunks: gemv_mma_kernel's per-k-step variant, so the sums run in the same order
+  if (!mlp_consume<T, 1, false>(D, rows_d, ring, full, empty, nst, j, part, pc_d, xs, false,
+                                skip))
+    return;
+  if (skip) return;
+  named_bar_sync(1, kConsumers);
+  {
+    T* y = static_cast<T*>(D.y);
+    const T* res = static_cast<const T*>(D.residual);
+    const int nrows = rows_d.y - rows_d.x;
+    for (int idx = tid; idx < nrows * D.batch; idx += kConsumers) {
+      const int b = idx / nrows, r = idx - b * nrows;
+      const int mt = r / 16, q = r - mt * 16;
+      float v = mlp_row_sum(part, nmt_d, pc_d, mt, q, b, D.batch, false);
+      const size_t o = (size_t)b * D.d_out + rows_d.x + r;
+      if (res != nullptr) v += Elem<T>::to_f(res[o]);
+      y[o] = Elem<T>::from_f(v);
+    }
+  }
+}
+
+// Shared bytes after the ring: the larger of the two phases' partials + activation.
+int mlp_region_bytes(int batch, int d_model, int d_ff, int G, bool split) {
+  const int rows_a = (d_ff + G - 1) / G, rows_d = (d_model + G - 1) / G;
+  const int pc_a = split ? 2 * batch : batch;
+  const size_t ra = (size_t)kConsumerWarps * ((rows_a + 7) / 8) * 16 * pc_a * 4 +
+                    (size_t)batch * d_model * 2 * (split ? 2 : 1);
+  const size_t rd = (size_t)kConsumerWarps * ((rows_d + 15) / 16) * 16 * batch * 4 +
+                    (size_t)batch * d_ff * 2;
+  return (int)((ra > rd ? ra : rd) + 15) & ~15;
+}
+
+template <typename T>
+int launch_mlp(MlpArgs m, cudaStream_t st, const DeviceInfo& dev) {
+  const bool split = m.g.gamma != nullptr;
+  const void* kern = split ? reinterpret_cast<const void*>(mlp_block_kernel<T, true>)
+                           : reinterpret_cast<const void*>(mlp_block_kernel<T, false>);
+  const size_t smem = (size_t)m.nstages * (kMmaStage + 16) + m.region_bytes;
+  if (int rc = allow_dynamic_smem(kern, dev, smem)) return rc;
+  return launch_pdl(kern, dim3(dev.num_sms), dim3(kThreads), smem, st, &m);
+}
+
+}  // namespace
+}  // namespace dbk
+
+extern "C" size_t dbk_mlp_block_workspace_bytes(void) { return 256; }
+
+extern "C" int dbk_mlp_block(const void* x, const void* gamma, const void* Wg, const void* Wu,
+                             const void* Wd, const void* residual, void* h, void* y, int batch,
+                             int d_model, int d_ff, float eps, int dtype, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (int rc = check_common(x, Wg, h, batch, d_model, d_ff, dtype)) return rc;
+  if (!Wu || !Wd || !y) return DBK_ENULL;
+  if (!aligned16(Wu) || !aligned16(Wd) || !aligned16(h) || (gamma && !aligned16(gamma)))
+    return DBK_EALIGN;
+  if (!workspace || workspace_bytes < dbk_mlp_block_workspace_bytes()) return DBK_EWORKSPACE;
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
+  // one CTA per SM owns rows of both GEMVs; the k-step order of each phase is that of
+  // gemv_mma_kernel for d_in <= 2 chunks (gate/up) and for d_in > 2 chunks (down)
+  if (batch > 4 || d_model % 16 != 0 || d_ff % 16 != 0 || d_model > 2 * kMmaKC ||
+      d_ff <= 2 * kMmaKC ||
+      d_model < dev.num_sms || d_ff < dev.num_sms)
+    return DBK_ESHAPE;
+  MlpArgs m{};
+  m.g.x = x; m.g.gamma = gamma; m.g.w0 = Wg; m.g.w1 = Wu; m.g.y = h;
+  m.g.batch = batch; m.g.d_in = d_model; m.g.d_out = d_ff; m.g.eps = eps;
+  m.g.nchunks = (d_model + kMmaKC - 1) / kMmaKC;
+  m.g.pcols = gamma ? 2 * batch : batch;
+  m.d.x = h; m.d.w0 = Wd; m.d.residual = residual; m.d.y = y;
+  m.d.batch = batch; m.d.d_in = d_ff; m.d.d_out = d_model;
+  m.d.nchunks = (d_ff + kMmaKC - 1) / kMmaKC;
+  m.d.pcols = batch;
+  m.sync = static_cast<int*>(workspace);
+  m.region_bytes = mlp_region_bytes(batch, d_model, d_ff, dev.num_sms, gamma != nullptr);
+  m.nstages = 0;
+  for (int nst = kMmaStages; nst >= 2; --nst)
+    if ((size_t)nst * (kMmaStage + 16) + m.region_bytes <= (size_t)dev.max_smem_optin - 1024) {
+      m.nstages = nst;
+      break;
+    }
+  if (m.nstages == 0) return DBK_ESHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == DBK_F16 ? launch_mlp<__half>(m, st, dev) : launch_mlp<__nv_bfloat16>(m, st, dev);
+}

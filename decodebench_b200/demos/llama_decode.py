@@ -270,8 +270,8 @@ def _build_layer(dim: int, batch: int, gen):
                                 inp["Kc"], inp["Vc"], H, Hkv, gamma=inp["g1"], eps=1e-5)
         o = ops.flashdecode(q, inp["Kc"], inp["Vc"], seq_lens=inp["lens"])
         h = ops.gemv(o.reshape(o.shape[0], -1), inp["Wo"], residual=inp["x"])
-        a = ops.gateup_swiglu(h, inp["Wg"], inp["Wu"], gamma=inp["g2"], eps=1e-5)
-        return ops.gemv(a, inp["Wd"], residual=h)
+        # RMSNorm + gate/up + SwiGLU, then down + residual: one persistent launch
+        return ops.mlp(h, inp["g2"], inp["Wg"], inp["Wu"], inp["Wd"], eps=1e-5, residual=h)
 
     inputs = {"x": x, "g1": g1, "g2": g2, "Wqkv": Wqkv, "Wqkv_il": Wqkv_il, "Wo": Wo, "Wg": Wg,
               "Wu": Wu, "Wd": Wd, "Kc": Kc, "Vc": Vc, "cos": cos, "sin": sin, "pos": pos,

@@ -12,6 +12,7 @@ missing kernel library, raises.
 from __future__ import annotations
 
 import math
+import os
 import threading
 
 import torch
@@ -260,11 +261,71 @@ def gemv(x: torch.Tensor, W: torch.Tensor, residual: torch.Tensor | None = None,
     return y
 
 
+_MLP_BLOCK = os.environ.get("DBK_MLP_BLOCK", "1") != "0"
+_mlp_block_refused: set = set()
+
+
 def mlp(x: torch.Tensor, gamma: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
         Wd: torch.Tensor, eps: float = 1e-5, residual: torch.Tensor | None = None) -> torch.Tensor:
-    """Decode MLP block: down(silu(gate(rmsnorm(x))) * up(rmsnorm(x))) (+ residual)."""
+    """Decode MLP block: down(silu(gate(rmsnorm(x))) * up(rmsnorm(x))) (+ residual).
+
+    One persistent launch (:func:`mlp_block`) where its shape rules allow, else
+    :func:`gateup_swiglu` then :func:`gemv`; the results are bit-identical.
+    ``DBK_MLP_BLOCK=0`` in the environment always takes the two launches."""
+    key = (x.device.index, x.dtype, x.numel() // x.shape[-1], x.shape[-1], Wg.shape[0])
+    if _MLP_BLOCK and key not in _mlp_block_refused:
+        try:
+            return mlp_block(x, Wg, Wu, Wd, gamma=gamma, eps=eps, residual=residual)
+        except N.DbkError as e:
+            if e.status != N.DBK_ESHAPE:
+                raise
+            _mlp_block_refused.add(key)      # refused before any launch
     h = gateup_swiglu(x, Wg, Wu, gamma=gamma, eps=eps)
     return gemv(h, Wd, residual=residual)
+
+
+def mlp_block(x: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor, Wd: torch.Tensor,
+              gamma: torch.Tensor | None = None, eps: float = 1e-5,
+              residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+              h: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The decode MLP block in one persistent launch (batch 1..4):
+    ``Wd @ (silu(Wg x') * (Wu x')) (+ residual)``, x' = RMSNorm(x) with ``gamma``.
+
+    Bit-identical to :func:`gateup_swiglu` followed by :func:`gemv`; the two
+    GEMVs meet at a grid-wide barrier inside the kernel instead of a kernel
+    boundary. ``h`` (optional, [batch, d_ff]) receives the intermediate
+    activation. Raises DbkError (DBK_ESHAPE) for shapes the single launch
+    does not cover (see ``dbk_mlp_block`` in dbk.h); :func:`mlp` covers all."""
+    dev = _need_cuda(x, Wg, Wu, Wd, gamma, residual)
+    _check_out(out, dev)
+    _check_out(h, dev)
+    dt = _dtype_code(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    batch, d_model = x2.shape
+    d_ff = Wg.shape[0]
+    if (Wg.shape != (d_ff, d_model) or Wu.shape != (d_ff, d_model)
+            or Wd.shape != (d_model, d_ff)):
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)}, Wg {tuple(Wg.shape)}, "
+                         f"Wu {tuple(Wu.shape)}, Wd {tuple(Wd.shape)}")
+    for t in (Wg, Wu, Wd, gamma, residual):
+        if t is not None and t.dtype != x.dtype:
+            raise TypeError("all operands must share one dtype")
+    if residual is not None and residual.numel() != batch * d_model:
+        raise ValueError("residual must have x's shape")
+    lib = N.load()
+    hbuf = h if h is not None else torch.empty(batch, d_ff, dtype=x.dtype, device=dev)
+    if hbuf.numel() != batch * d_ff or not hbuf.is_contiguous():
+        raise ValueError("h must be a contiguous [batch, d_ff] tensor")
+    y = out if out is not None else torch.empty_like(x)
+    ws = _workspace(("mlp_block",), lib.dbk_mlp_block_workspace_bytes(), dev, workspace)
+    x2 = x2.contiguous()
+    r = residual.contiguous() if residual is not None else None
+    N.check("dbk_mlp_block", lib.dbk_mlp_block(
+        x2.data_ptr(), _ptr(gamma), Wg.data_ptr(), Wu.data_ptr(), Wd.data_ptr(), _ptr(r),
+        hbuf.data_ptr(), y.data_ptr(), batch, d_model, d_ff, float(eps), dt, ws.data_ptr(),
+        ws.numel(), _stream(dev)))
+    return y
 
 
 def flashdecode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,

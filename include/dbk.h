@@ -118,6 +118,30 @@ int dbk_gemv(const void* x, const void* W, const void* residual, void* y,
              int batch, int d_in, int d_out, int dtype,
              void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode MLP block in ONE persistent launch (batch 1..4):
+ *   h = silu(Wg x') * (Wu x'), x' = x or, when gamma is not NULL, RMSNorm(x);
+ *   y = Wd h (+ residual when not NULL).
+ * x, residual, y [batch, d_model]; Wg, Wu [d_ff, d_model]; Wd [d_model, d_ff];
+ * h [batch, d_ff] is written (the intermediate activation, caller-owned).
+ * One CTA per SM computes its rows of h, meets the other CTAs at a grid-wide
+ * barrier (bounded wait; two counters in `workspace`), then its rows of y,
+ * while the down weights stream in behind the gate/up weights without a
+ * kernel boundary. Bit-identical to dbk_gateup_swiglu followed by dbk_gemv.
+ * workspace: >= dbk_mlp_block_workspace_bytes() bytes, zero-filled before the
+ * first call (every call leaves it zero); one per call that may run
+ * concurrently. All CTAs must be resident at once: do not run it beside a
+ * kernel that holds SMs until this one finishes. DBK_ESHAPE unless
+ * d_model % 16 == 0, d_ff % 16 == 0, SM count <= d_model <= 4096 and
+ * d_ff > 4096 and both phases' activation stage fits in shared memory (three
+ * weight-ring stages up to batch * d_ff of about 16,000, two up to about 49,000). Replaces the f2_kernel launch plus the down-projection launch
+ * (validation/src/kernels/fused/f2.cu:17-76, bench_variant.cu:562-575;
+ * src/decodebench/demos/llama_decode.py:77-87) with one launch. */
+int dbk_mlp_block(const void* x, const void* gamma, const void* Wg, const void* Wu,
+                  const void* Wd, const void* residual, void* h, void* y, int batch,
+                  int d_model, int d_ff, float eps, int dtype, void* workspace,
+                  size_t workspace_bytes, void* stream);
+size_t dbk_mlp_block_workspace_bytes(void);
+
 /* F4: split-KV FlashDecode, one query token per sequence.
  *   q   [batch, n_q_heads, head_dim]
  *   out [batch, n_q_heads, head_dim]

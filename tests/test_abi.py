@@ -46,6 +46,14 @@ def test_null_and_shape_errors_before_any_device_work():
                                None, 0, None) == -2                              # 3 % 2
     assert lib.dbk_flashdecode(16, 16, 16, None, None, 16, 1, 2, 2, 64, 64, 0, 0, 1.0, 0, 0,
                                None, 0, None) == -2                              # head_dim
+    # dbk_mlp_block: x, Wg, Wu, Wd, residual, h, y ... workspace, bytes, stream
+    assert lib.dbk_mlp_block_workspace_bytes() >= 8
+    assert lib.dbk_mlp_block(16, None, 16, None, 16, None, 16, 16, 1, 1024, 4352, 1e-5, 0,
+                             16, 256, None) == -1                               # Wu
+    assert lib.dbk_mlp_block(16, None, 16, 16, 24, None, 16, 16, 1, 1024, 4352, 1e-5, 0,
+                             16, 256, None) == -3                               # misaligned Wd
+    assert lib.dbk_mlp_block(16, None, 16, 16, 16, None, 16, 16, 1, 1024, 4352, 1e-5, 0,
+                             None, 0, None) == -4                               # no workspace
 
 
 def test_ops_refuse_cpu_tensors():
