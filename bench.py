@@ -892,9 +892,11 @@ class Layer(Workload):
         self.out = None
         from decodebench_b200 import ops
 
-        # the MLP block is one persistent launch unless DBK_MLP_BLOCK=0
+        # the MLP block is one persistent launch unless DBK_MLP_BLOCK=0 (o_proj joins it
+        # with DBK_LAYER_TAIL=1)
         self.fused(self.reps[0])
-        self.kernels_per_step = 4 if ops._MLP_BLOCK and not ops._mlp_block_refused else 5
+        if ops._MLP_BLOCK and not ops._mlp_block_refused:
+            self.kernels_per_step = 3 if ops._LAYER_TAIL else 4
 
     def describe(self):
         return {"workload": "whole Llama decode layer, d 4096, 32 q / 8 kv heads, FFN 11008, fp16, "

@@ -35,6 +35,8 @@ SIGNATURES = {
     "dbk_gemv": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
     "dbk_mlp_block": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P, _SZ, _P]),
     "dbk_mlp_block_workspace_bytes": (_SZ, []),
+    "dbk_oproj_mlp_block": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I,
+                                 _P, _SZ, _P]),
     "dbk_flashdecode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,
                              _P, _SZ, _P]),
     "dbk_flashdecode_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I,

@@ -1032,9 +1032,10 @@ namespace dbk {
 namespace {
 
 struct MlpArgs {
+  GemvArgs o;        // optional phase 0: MODE_PLAIN, y = h_attn = Wo o + residual
   GemvArgs g;        // phase 1: MODE_SWIGLU, y = h
   GemvArgs d;        // phase 2: MODE_PLAIN, x = h, with residual
-  int* sync;         // [2]: arrivals, departures (zero before and after a launch)
+  int* sync;         // [2 per barrier]: arrivals, departures (zero before and after a launch)
   int nstages;
   int region_bytes;  // shared bytes after the ring shared by the two phases
 };
@@ -1178,7 +1179,56 @@ __device__ __forceinline__ float mlp_row_sum(const float* part, int nmt, int pc,
   return t;
 }
 
-template <typename T, bool SPLIT>
+// A phase y = W x (+ residual) of the persistent kernel (MODE_PLAIN): stages x
+// (written by this launch when in_kernel: read through L2, not the non-coherent
+// path), runs the ring, adds the 8 warp partials and the residual, stores y.
+// The k-step order is gemv_mma_kernel's for the same d_in. False when a bounded
+// wait gave up; with skip it only drains its stages.
+template <typename T>
+__device__ __forceinline__ bool mlp_plain_phase(const GemvArgs& P, uint8_t* region,
+                                                const uint8_t* ring, uint64_t* full,
+                                                uint64_t* empty, int nst, int& j, bool in_kernel,
+                                                bool skip) {
+  const int tid = threadIdx.x;
+  const int2 rows = cta_rows(P.d_out, gridDim.x);
+  const int nmt = (rows.y - rows.x + 15) / 16;
+  const int pc = P.batch;
+  float* part = reinterpret_cast<float*>(region);
+  uint16_t* xs = reinterpret_cast<uint16_t*>(part + (size_t)kConsumerWarps * nmt * 16 * pc);
+  if (!skip) {
+    const uint4* src = static_cast<const uint4*>(P.x);
+    for (int v = tid; v < P.batch * P.d_in / 8; v += kConsumers)
+      reinterpret_cast<uint4*>(xs)[v] = in_kernel ? __ldcg(src + v) : ldg_nc_v4(src + v);
+  }
+  named_bar_sync(1, kConsumers);
+  const bool ok =
+      P.nchunks <= 2
+          ? mlp_consume<T, 1, true>(P, rows, ring, full, empty, nst, j, part, pc, xs, false, skip)
+          : mlp_consume<T, 1, false>(P, rows, ring, full, empty, nst, j, part, pc, xs, false, skip);
+  if (!ok) return false;
+  if (skip) return true;
+  named_bar_sync(1, kConsumers);
+  T* y = static_cast<T*>(P.y);
+  const unsigned short* res = static_cast<const unsigned short*>(P.residual);
+  const int nrows = rows.y - rows.x;
+  for (int idx = tid; idx < nrows * P.batch; idx += kConsumers) {
+    const int b = idx / nrows, r = idx - b * nrows;
+    const int mt = r / 16, q = r - mt * 16;
+    float v = mlp_row_sum(part, nmt, pc, mt, q, b, P.batch, false);
+    const size_t o = (size_t)b * P.d_out + rows.x + r;
+    if (res != nullptr) {
+      const unsigned short u = __ldcg(res + o);      // may have been written by this launch
+      v += Elem<T>::to_f(*reinterpret_cast<const T*>(&u));
+    }
+    y[o] = Elem<T>::from_f(v);
+  }
+  named_bar_sync(1, kConsumers);      // the partials are read before the region is reused
+  return true;
+}
+
+// PRE: a phase 0 first, h_attn = Wo o + residual (the attention output
+// projection), whose output is phase 1's x and phase 2's residual.
+template <typename T, bool SPLIT, bool PRE>
 __global__ void __launch_bounds__(kThreads, 1) mlp_block_kernel(const MlpArgs m) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const int nst = m.nstages;
@@ -1194,7 +1244,6 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_block_kernel(const MlpArgs m)
   const GemvArgs& D = m.d;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
-  const int2 rows_a = cta_rows(A.d_out, G);
 
   if (tid == 0) {
     for (int s = 0; s < nst; ++s) {
@@ -1210,20 +1259,39 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_block_kernel(const MlpArgs m)
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       int j = 0;
-      if (mlp_produce<2>(A, rows_a, ring, full, empty, nst, j, pol))
+      if ((!PRE || mlp_produce<1>(m.o, cta_rows(m.o.d_out, G), ring, full, empty, nst, j, pol)) &&
+          mlp_produce<2>(A, cta_rows(A.d_out, G), ring, full, empty, nst, j, pol))
         mlp_produce<1>(D, cta_rows(D.d_out, G), ring, full, empty, nst, j, pol);
     }
     return;
   }
 
-  // -------------------------------------------------- phase 1: gate/up + SwiGLU
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  int j = 0;
+  int barrier = 0;
+  // Every output store of this CTA precedes its arrival at the grid-wide barrier.
+  auto meet = [&]() {
+    named_bar_sync(1, kConsumers);
+    if (tid == 0) s_ok = grid_barrier(m.sync + 2 * barrier, G) ? 1 : 0;
+    ++barrier;
+    named_bar_sync(1, kConsumers);
+    return s_ok != 0;
+  };
+  bool skip = false;
+  // ------------------------------------------- phase 0: o_proj (+ residual)
+  if constexpr (PRE) {
+    if (!mlp_plain_phase<T>(m.o, region, ring, full, empty, nst, j, false, false)) return;
+    skip = !meet();
+  }
+
+  // -------------------------------------------------- phase 1: gate/up + SwiGLU
+  const int2 rows_a = cta_rows(A.d_out, G);
   const int nmt_a = (rows_a.y - rows_a.x + 7) / 8;
   const int pc_a = A.pcols;
   const bool packed_a = SPLIT && pc_a > A.batch;
   float* part = reinterpret_cast<float*>(region);
   uint16_t* xs = reinterpret_cast<uint16_t*>(part + (size_t)kConsumerWarps * nmt_a * 16 * pc_a);
-  {
+  if (!skip) {
     const T* x = static_cast<const T*>(A.x);
     const T* gam = static_cast<const T*>(A.gamma);
     uint16_t* xs_lo = xs + (size_t)A.batch * A.d_in;
@@ -1233,8 +1301,9 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_block_kernel(const MlpArgs m)
     const int per_row = A.d_in / 8;
     for (int v = tid; v < A.batch * per_row; v += kConsumers) {
       const int b = v / per_row, c = (v - b * per_row) * 8;
+      const uint4* xv = reinterpret_cast<const uint4*>(x + (size_t)b * A.d_in + c);
       float f[8], g[8];
-      unpack8<T>(ldg_nc_v4(x + (size_t)b * A.d_in + c), f);
+      unpack8<T>(PRE ? __ldcg(xv) : ldg_nc_v4(xv), f);      // phase 0 wrote x when PRE
       if (gam != nullptr) unpack8<T>(ldg_nc_v4(gam + c), g);
       uint32_t hi[4], lo[4];
       float sq = 0.f;
@@ -1262,19 +1331,18 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_block_kernel(const MlpArgs m)
   named_bar_sync(1, kConsumers);
   if (tid < 8) {
     float v = 1.f;
-    if (A.gamma != nullptr && tid < A.batch) {
+    if (!skip && A.gamma != nullptr && tid < A.batch) {
       float t = 0.f;
       for (int w = 0; w < kConsumerWarps; ++w) t += red[w][tid];
       v = rsqrtf(t / (float)A.d_in + A.eps);
     }
     inv_rms[tid] = v;
   }
-  int j = 0;
   if (!mlp_consume<T, 2, true>(A, rows_a, ring, full, empty, nst, j, part, pc_a, xs, packed_a,
-                               false))
+                               skip))
     return;
   named_bar_sync(1, kConsumers);
-  {
+  if (!skip) {
     T* h = static_cast<T*>(A.y);
     const int nrows = rows_a.y - rows_a.x;
     for (int idx = tid; idx < nrows * A.batch; idx += kConsumers) {
@@ -1285,70 +1353,92 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_block_kernel(const MlpArgs m)
                       (mlp_row_sum(part, nmt_a, pc_a, mt, 8 + q, b, A.batch, packed_a) * sc);
       h[(size_t)b * A.d_out + rows_a.x + r] = Elem<T>::from_f(v);
     }
+    skip = !meet();
   }
-  named_bar_sync(1, kConsumers);      // every h store of this CTA precedes the barrier
-  if (tid == 0) s_ok = grid_barrier(m.sync, G) ? 1 : 0;
-  named_bar_sync(1, kConsumers);
-  const bool skip = s_ok == 0;
 
   // -------------------------------------------------- phase 2: down (+ residual)
-  const int2 rows_d = cta_rows(D.d_out, G);
-  const int nmt_d = (rows_d.y - rows_d.x + 15) / 16;
-  const int pc_d = D.batch;
-  xs = reinterpret_cast<uint16_t*>(part + (size_t)kConsumerWarps * nmt_d * 16 * pc_d);
-  if (!skip) {
-    // h was written by this launch: read it through L2 (not the non-coherent path)
-    const uint4* src = static_cast<const uint4*>(D.x);
-    for (int v = tid; v < D.batch * D.d_in / 8; v += kConsumers)
-      reinterpret_cast<uint4*>(xs)[v] = __ldcg(src + v);
-  }
-  named_bar_sync(1, kConsumers);
-  // d_ff > 2 chunks: gemv_mma_kernel's per-k-step variant, so the sums run in the same order
-  if (!mlp_consume<T, 1, false>(D, rows_d, ring, full, empty, nst, j, part, pc_d, xs, false,
-                                skip))
-    return;
-  if (skip) return;
-  named_bar_sync(1, kConsumers);
-  {
-    T* y = static_cast<T*>(D.y);
-    const T* res = static_cast<const T*>(D.residual);
-    const int nrows = rows_d.y - rows_d.x;
-    for (int idx = tid; idx < nrows * D.batch; idx += kConsumers) {
-      const int b = idx / nrows, r = idx - b * nrows;
-      const int mt = r / 16, q = r - mt * 16;
-      float v = mlp_row_sum(part, nmt_d, pc_d, mt, q, b, D.batch, false);
-      const size_t o = (size_t)b * D.d_out + rows_d.x + r;
-      if (res != nullptr) v += Elem<T>::to_f(res[o]);
-      y[o] = Elem<T>::from_f(v);
-    }
-  }
+  // (d_ff > 2 chunks: gemv_mma_kernel's per-k-step variant, so the sums run in the same order)
+  mlp_plain_phase<T>(D, region, ring, full, empty, nst, j, true, skip);
 }
 
-// Shared bytes after the ring: the larger of the two phases' partials + activation.
-int mlp_region_bytes(int batch, int d_model, int d_ff, int G, bool split) {
-  const int rows_a = (d_ff + G - 1) / G, rows_d = (d_model + G - 1) / G;
+// Shared bytes after the ring: the largest phase's partials + activation stage.
+int mlp_region_bytes(int batch, int d_attn, int d_model, int d_ff, int G, bool split) {
+  auto plain = [&](int d_in, int d_out) {
+    return (size_t)kConsumerWarps * (((d_out + G - 1) / G + 15) / 16) * 16 * batch * 4 +
+           (size_t)batch * d_in * 2;
+  };
   const int pc_a = split ? 2 * batch : batch;
-  const size_t ra = (size_t)kConsumerWarps * ((rows_a + 7) / 8) * 16 * pc_a * 4 +
+  const size_t ra = (size_t)kConsumerWarps * (((d_ff + G - 1) / G + 7) / 8) * 16 * pc_a * 4 +
                     (size_t)batch * d_model * 2 * (split ? 2 : 1);
-  const size_t rd = (size_t)kConsumerWarps * ((rows_d + 15) / 16) * 16 * batch * 4 +
-                    (size_t)batch * d_ff * 2;
-  return (int)((ra > rd ? ra : rd) + 15) & ~15;
+  size_t r = ra > plain(d_ff, d_model) ? ra : plain(d_ff, d_model);
+  if (d_attn > 0 && plain(d_attn, d_model) > r) r = plain(d_attn, d_model);
+  return (int)((r + 15) & ~(size_t)15);
 }
 
-template <typename T>
+template <typename T, bool PRE>
 int launch_mlp(MlpArgs m, cudaStream_t st, const DeviceInfo& dev) {
   const bool split = m.g.gamma != nullptr;
-  const void* kern = split ? reinterpret_cast<const void*>(mlp_block_kernel<T, true>)
-                           : reinterpret_cast<const void*>(mlp_block_kernel<T, false>);
+  const void* kern = split ? reinterpret_cast<const void*>(mlp_block_kernel<T, true, PRE>)
+                           : reinterpret_cast<const void*>(mlp_block_kernel<T, false, PRE>);
   const size_t smem = (size_t)m.nstages * (kMmaStage + 16) + m.region_bytes;
   if (int rc = allow_dynamic_smem(kern, dev, smem)) return rc;
   return launch_pdl(kern, dim3(dev.num_sms), dim3(kThreads), smem, st, &m);
 }
 
+// Shared checks and set-up of both entry points; d_attn = 0 without phase 0.
+int mlp_launch(MlpArgs& m, int batch, int d_attn, int d_model, int d_ff, int dtype,
+               void* workspace, size_t workspace_bytes, void* stream);
+
 }  // namespace
 }  // namespace dbk
 
 extern "C" size_t dbk_mlp_block_workspace_bytes(void) { return 256; }
+
+namespace dbk {
+namespace {
+int mlp_launch(MlpArgs& m, int batch, int d_attn, int d_model, int d_ff, int dtype,
+               void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace || workspace_bytes < dbk_mlp_block_workspace_bytes()) return DBK_EWORKSPACE;
+  DeviceInfo dev;
+  if (int rc = current_device_info(&dev)) return rc;
+  // one CTA per SM owns rows of every GEMV (d_model, d_ff >= the SM count); gate/up
+  // caches nothing in registers but keeps the two-chain k-step order of
+  // gemv_mma_kernel's variant for d_in <= 2 chunks
+  if (batch > 4 || d_model % 16 != 0 || d_ff % 16 != 0 || d_attn % 16 != 0 ||
+      d_model > 2 * kMmaKC || d_model < dev.num_sms || d_ff < dev.num_sms)
+    return DBK_ESHAPE;
+  auto chunks = [](int d_in) { return (d_in + kMmaKC - 1) / kMmaKC; };
+  m.g.batch = batch; m.g.d_in = d_model; m.g.d_out = d_ff;
+  m.g.nchunks = chunks(d_model);
+  m.g.pcols = m.g.gamma ? 2 * batch : batch;
+  m.d.x = m.g.y;
+  m.d.batch = batch; m.d.d_in = d_ff; m.d.d_out = d_model;
+  m.d.nchunks = chunks(d_ff);
+  m.d.pcols = batch;
+  if (d_attn > 0) {
+    m.o.batch = batch; m.o.d_in = d_attn; m.o.d_out = d_model;
+    m.o.nchunks = chunks(d_attn);
+    m.o.pcols = batch;
+  }
+  m.sync = static_cast<int*>(workspace);
+  m.region_bytes = mlp_region_bytes(batch, d_attn, d_model, d_ff, dev.num_sms,
+                                    m.g.gamma != nullptr);
+  m.nstages = 0;
+  for (int nst = kMmaStages; nst >= 2; --nst)
+    if ((size_t)nst * (kMmaStage + 16) + m.region_bytes <= (size_t)dev.max_smem_optin - 1024) {
+      m.nstages = nst;
+      break;
+    }
+  if (m.nstages == 0) return DBK_ESHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (d_attn > 0)
+    return dtype == DBK_F16 ? launch_mlp<__half, true>(m, st, dev)
+                            : launch_mlp<__nv_bfloat16, true>(m, st, dev);
+  return dtype == DBK_F16 ? launch_mlp<__half, false>(m, st, dev)
+                          : launch_mlp<__nv_bfloat16, false>(m, st, dev);
+}
+}  // namespace
+}  // namespace dbk
 
 extern "C" int dbk_mlp_block(const void* x, const void* gamma, const void* Wg, const void* Wu,
                              const void* Wd, const void* residual, void* h, void* y, int batch,
@@ -1358,33 +1448,26 @@ extern "C" int dbk_mlp_block(const void* x, const void* gamma, const void* Wg, c
   if (!Wu || !Wd || !y) return DBK_ENULL;
   if (!aligned16(Wu) || !aligned16(Wd) || !aligned16(h) || (gamma && !aligned16(gamma)))
     return DBK_EALIGN;
-  if (!workspace || workspace_bytes < dbk_mlp_block_workspace_bytes()) return DBK_EWORKSPACE;
-  DeviceInfo dev;
-  if (int rc = current_device_info(&dev)) return rc;
-  // one CTA per SM owns rows of both GEMVs; the k-step order of each phase is that of
-  // gemv_mma_kernel for d_in <= 2 chunks (gate/up) and for d_in > 2 chunks (down)
-  if (batch > 4 || d_model % 16 != 0 || d_ff % 16 != 0 || d_model > 2 * kMmaKC ||
-      d_ff <= 2 * kMmaKC ||
-      d_model < dev.num_sms || d_ff < dev.num_sms)
-    return DBK_ESHAPE;
   MlpArgs m{};
-  m.g.x = x; m.g.gamma = gamma; m.g.w0 = Wg; m.g.w1 = Wu; m.g.y = h;
-  m.g.batch = batch; m.g.d_in = d_model; m.g.d_out = d_ff; m.g.eps = eps;
-  m.g.nchunks = (d_model + kMmaKC - 1) / kMmaKC;
-  m.g.pcols = gamma ? 2 * batch : batch;
-  m.d.x = h; m.d.w0 = Wd; m.d.residual = residual; m.d.y = y;
-  m.d.batch = batch; m.d.d_in = d_ff; m.d.d_out = d_model;
-  m.d.nchunks = (d_ff + kMmaKC - 1) / kMmaKC;
-  m.d.pcols = batch;
-  m.sync = static_cast<int*>(workspace);
-  m.region_bytes = mlp_region_bytes(batch, d_model, d_ff, dev.num_sms, gamma != nullptr);
-  m.nstages = 0;
-  for (int nst = kMmaStages; nst >= 2; --nst)
-    if ((size_t)nst * (kMmaStage + 16) + m.region_bytes <= (size_t)dev.max_smem_optin - 1024) {
-      m.nstages = nst;
-      break;
-    }
-  if (m.nstages == 0) return DBK_ESHAPE;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return dtype == DBK_F16 ? launch_mlp<__half>(m, st, dev) : launch_mlp<__nv_bfloat16>(m, st, dev);
+  m.g.x = x; m.g.gamma = gamma; m.g.w0 = Wg; m.g.w1 = Wu; m.g.y = h; m.g.eps = eps;
+  m.d.w0 = Wd; m.d.residual = residual; m.d.y = y;
+  return mlp_launch(m, batch, 0, d_model, d_ff, dtype, workspace, workspace_bytes, stream);
+}
+
+extern "C" int dbk_oproj_mlp_block(const void* attn, const void* Wo, const void* x,
+                                   const void* gamma, const void* Wg, const void* Wu,
+                                   const void* Wd, void* h_attn, void* h, void* y, int batch,
+                                   int d_attn, int d_model, int d_ff, float eps, int dtype,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_common(attn, Wo, h_attn, batch, d_attn, d_model, dtype)) return rc;
+  if (int rc = check_common(h_attn, Wg, h, batch, d_model, d_ff, dtype)) return rc;
+  if (!x || !Wu || !Wd || !y) return DBK_ENULL;
+  if (!aligned16(Wu) || !aligned16(Wd) || !aligned16(h) || !aligned16(h_attn) ||
+      (gamma && !aligned16(gamma)))
+    return DBK_EALIGN;
+  MlpArgs m{};
+  m.o.x = attn; m.o.w0 = Wo; m.o.residual = x; m.o.y = h_attn;
+  m.g.x = h_attn; m.g.gamma = gamma; m.g.w0 = Wg; m.g.w1 = Wu; m.g.y = h; m.g.eps = eps;
+  m.d.w0 = Wd; m.d.residual = h_attn; m.d.y = y;
+  return mlp_launch(m, batch, d_attn, d_model, d_ff, dtype, workspace, workspace_bytes, stream);
 }

@@ -269,9 +269,10 @@ def _build_layer(dim: int, batch: int, gen):
         q = ops.qkv_rope_append(inp["x"], inp["Wqkv_il"], inp["pos"], inp["inv_freq"],
                                 inp["Kc"], inp["Vc"], H, Hkv, gamma=inp["g1"], eps=1e-5)
         o = ops.flashdecode(q, inp["Kc"], inp["Vc"], seq_lens=inp["lens"])
-        h = ops.gemv(o.reshape(o.shape[0], -1), inp["Wo"], residual=inp["x"])
-        # RMSNorm + gate/up + SwiGLU, then down + residual: one persistent launch
-        return ops.mlp(h, inp["g2"], inp["Wg"], inp["Wu"], inp["Wd"], eps=1e-5, residual=h)
+        # o_proj + residual, then RMSNorm + gate/up + SwiGLU and down + residual in one
+        # persistent launch
+        return ops.layer_tail(o.reshape(o.shape[0], -1), inp["Wo"], inp["x"], inp["g2"],
+                              inp["Wg"], inp["Wu"], inp["Wd"], eps=1e-5)
 
     inputs = {"x": x, "g1": g1, "g2": g2, "Wqkv": Wqkv, "Wqkv_il": Wqkv_il, "Wo": Wo, "Wg": Wg,
               "Wu": Wu, "Wd": Wd, "Kc": Kc, "Vc": Vc, "cos": cos, "sin": sin, "pos": pos,

@@ -328,6 +328,74 @@ def mlp_block(x: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor, Wd: torch.Ten
     return y
 
 
+def oproj_mlp_block(attn: torch.Tensor, Wo: torch.Tensor, x: torch.Tensor, Wg: torch.Tensor,
+                    Wu: torch.Tensor, Wd: torch.Tensor, gamma: torch.Tensor | None = None,
+                    eps: float = 1e-5, out: torch.Tensor | None = None,
+                    h_attn: torch.Tensor | None = None, h: torch.Tensor | None = None,
+                    workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The rest of a decode layer after attention, in one persistent launch:
+    ``h_attn = attn Wo^T + x``, then :func:`mlp_block` on h_attn with h_attn as
+    the residual. Bit-identical to :func:`gemv` followed by :func:`mlp_block`.
+    ``h_attn`` / ``h`` (optional) receive the two intermediate activations.
+    Raises DbkError (DBK_ESHAPE) outside the single launch's shape rules;
+    :func:`layer_tail` covers all shapes."""
+    dev = _need_cuda(attn, Wo, x, Wg, Wu, Wd, gamma)
+    _check_out(out, dev)
+    dt = _dtype_code(x)
+    a2 = attn.reshape(x.numel() // x.shape[-1], -1)
+    batch, d_attn = a2.shape
+    d_model = x.shape[-1]
+    d_ff = Wg.shape[0]
+    if (Wo.shape != (d_model, d_attn) or Wg.shape != (d_ff, d_model)
+            or Wu.shape != (d_ff, d_model) or Wd.shape != (d_model, d_ff)):
+        raise ValueError(f"shape mismatch: attn {tuple(attn.shape)}, Wo {tuple(Wo.shape)}, "
+                         f"x {tuple(x.shape)}, Wg {tuple(Wg.shape)}, Wd {tuple(Wd.shape)}")
+    for t in (attn, Wo, Wg, Wu, Wd, gamma):
+        if t is not None and t.dtype != x.dtype:
+            raise TypeError("all operands must share one dtype")
+    lib = N.load()
+    ha = h_attn if h_attn is not None else torch.empty(batch, d_model, dtype=x.dtype, device=dev)
+    hb = h if h is not None else torch.empty(batch, d_ff, dtype=x.dtype, device=dev)
+    for t, n in ((ha, batch * d_model), (hb, batch * d_ff)):
+        if t.numel() != n or not t.is_contiguous() or not t.is_cuda:
+            raise ValueError("h_attn / h must be contiguous CUDA tensors of [batch, d_model] / "
+                             "[batch, d_ff] elements")
+    y = out if out is not None else torch.empty_like(x)
+    ws = _workspace(("mlp_block",), lib.dbk_mlp_block_workspace_bytes(), dev, workspace)
+    N.check("dbk_oproj_mlp_block", lib.dbk_oproj_mlp_block(
+        a2.data_ptr(), Wo.data_ptr(), x.data_ptr(), _ptr(gamma), Wg.data_ptr(), Wu.data_ptr(),
+        Wd.data_ptr(), ha.data_ptr(), hb.data_ptr(), y.data_ptr(), batch, d_attn, d_model, d_ff,
+        float(eps), dt, ws.data_ptr(), ws.numel(), _stream(dev)))
+    return y
+
+
+_LAYER_TAIL = os.environ.get("DBK_LAYER_TAIL", "0") == "1"
+
+
+def layer_tail(attn: torch.Tensor, Wo: torch.Tensor, x: torch.Tensor, gamma: torch.Tensor,
+               Wg: torch.Tensor, Wu: torch.Tensor, Wd: torch.Tensor,
+               eps: float = 1e-5) -> torch.Tensor:
+    """o_proj + residual, then the MLP block with that result as its residual.
+
+    By default :func:`gemv` then :func:`mlp` (two launches: on one B200 the
+    decode layer measured faster this way than with o_proj inside the
+    persistent kernel, whose launch then waits for the attention kernel's SMs
+    before any Wo byte moves). ``DBK_LAYER_TAIL=1`` in the environment takes
+    the single launch (:func:`oproj_mlp_block`) where its shape rules allow. The
+    results are bit-identical either way."""
+    if _LAYER_TAIL and _MLP_BLOCK:
+        key = ("tail", x.device.index, x.dtype, tuple(attn.shape), tuple(x.shape), Wg.shape[0])
+        if key not in _mlp_block_refused:
+            try:
+                return oproj_mlp_block(attn, Wo, x, Wg, Wu, Wd, gamma=gamma, eps=eps)
+            except N.DbkError as e:
+                if e.status != N.DBK_ESHAPE:
+                    raise
+                _mlp_block_refused.add(key)      # refused before any launch
+    h = gemv(attn.reshape(x.numel() // x.shape[-1], -1), Wo, residual=x)
+    return mlp(h, gamma, Wg, Wu, Wd, eps=eps, residual=h)
+
+
 def flashdecode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                 seq_lens: torch.Tensor | None = None, page_table: torch.Tensor | None = None,
                 scale: float | None = None, split_tokens: int = 0,

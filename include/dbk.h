@@ -131,16 +131,30 @@ int dbk_gemv(const void* x, const void* W, const void* residual, void* y,
  * first call (every call leaves it zero); one per call that may run
  * concurrently. All CTAs must be resident at once: do not run it beside a
  * kernel that holds SMs until this one finishes. DBK_ESHAPE unless
- * d_model % 16 == 0, d_ff % 16 == 0, SM count <= d_model <= 4096 and
- * d_ff > 4096 and both phases' activation stage fits in shared memory (three
- * weight-ring stages up to batch * d_ff of about 16,000, two up to about 49,000). Replaces the f2_kernel launch plus the down-projection launch
- * (validation/src/kernels/fused/f2.cu:17-76, bench_variant.cu:562-575;
+ * d_model % 16 == 0, d_ff % 16 == 0, SM count <= d_model <= 4096,
+ * d_ff >= SM count and every phase's activation stage fits in shared memory
+ * (with three weight-ring stages up to batch * d_ff of about 16,000, with two
+ * up to about 49,000). Replaces the f2_kernel launch plus the down-projection
+ * launch (validation/src/kernels/fused/f2.cu:17-76, bench_variant.cu:562-575;
  * src/decodebench/demos/llama_decode.py:77-87) with one launch. */
 int dbk_mlp_block(const void* x, const void* gamma, const void* Wg, const void* Wu,
                   const void* Wd, const void* residual, void* h, void* y, int batch,
                   int d_model, int d_ff, float eps, int dtype, void* workspace,
                   size_t workspace_bytes, void* stream);
 size_t dbk_mlp_block_workspace_bytes(void);
+
+/* The rest of a decode layer after attention, in ONE persistent launch:
+ *   h_attn = Wo attn + x;  y = dbk_mlp_block(h_attn, gamma, Wg, Wu, Wd, residual = h_attn).
+ * attn [batch, d_attn] (the attention output, heads concatenated); Wo
+ * [d_model, d_attn]; h_attn and h are written (caller-owned). Two grid-wide
+ * barriers; the Wg/Wu and Wd streams start behind Wo's. Bit-identical to
+ * dbk_gemv(attn, Wo, x) followed by dbk_mlp_block. Same rules as
+ * dbk_mlp_block, plus d_attn % 16 == 0. No counterpart in the reference (its
+ * demos stop at single stages, src/decodebench/demos/llama_decode.py). */
+int dbk_oproj_mlp_block(const void* attn, const void* Wo, const void* x, const void* gamma,
+                        const void* Wg, const void* Wu, const void* Wd, void* h_attn, void* h,
+                        void* y, int batch, int d_attn, int d_model, int d_ff, float eps,
+                        int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
 /* F4: split-KV FlashDecode, one query token per sequence.
  *   q   [batch, n_q_heads, head_dim]

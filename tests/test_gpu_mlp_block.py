@@ -7,7 +7,9 @@ barrier, then down + residual, in one launch.
 * bit for bit against the two-launch chain dbk_gateup_swiglu -> dbk_gemv, whose
   per-output summation order it keeps;
 * the workspace's barrier counters are zero again after every call, so calls
-  repeat; shapes outside the single launch are refused with DBK_ESHAPE."""
+  repeat; shapes outside the single launch are refused with DBK_ESHAPE;
+* dbk_oproj_mlp_block (o_proj + residual, then the block: two grid barriers)
+  the same way, against dbk_gemv followed by dbk_mlp_block and the oracle."""
 
 from __future__ import annotations
 
@@ -43,6 +45,7 @@ def _t(a, dt):
     (2, 2048, 5632, O.F16, True, False),
     (3, 1024, 4352, O.BF16, False, True),     # no RMSNorm: x is used as is
     (4, 2048, 5632, O.F16, True, True),       # two ring stages
+    (2, 1024, 2816, O.F16, True, True),       # d_ff <= 2 chunks: down keeps two chains
 ])
 def test_mlp_block_matches_oracle_and_chain(batch, d, ff, dt, gamma, residual):
     from decodebench_b200 import ops
@@ -93,7 +96,7 @@ def test_mlp_block_repeats_and_leaves_workspace_zero():
     assert int(ws.count_nonzero()) == 0
 
 
-@pytest.mark.parametrize("batch,d,ff", [(5, 1024, 4352), (1, 1024, 4096), (1, 8192, 11008)])
+@pytest.mark.parametrize("batch,d,ff", [(5, 1024, 4352), (1, 128, 4352), (1, 8192, 11008)])
 def test_mlp_block_refuses_shapes_outside_one_launch(batch, d, ff):
     from decodebench_b200 import _native as N
     from decodebench_b200 import ops
@@ -101,3 +104,33 @@ def test_mlp_block_refuses_shapes_outside_one_launch(batch, d, ff):
     t = lambda *s: torch.zeros(*s, dtype=torch.float16, device="cuda")  # noqa: E731
     with pytest.raises(N.DbkError, match="status -2"):
         ops.mlp_block(t(batch, d), t(ff, d), t(ff, d), t(d, ff), gamma=t(d))
+
+
+@pytest.mark.parametrize("batch,d_attn,d,ff,dt", [
+    (1, 4096, 4096, 11008, O.F16),     # the decode layer's tail (Llama-2-7B shape)
+    (2, 2048, 2048, 5632, O.BF16),
+    (3, 1024, 1024, 4352, O.F16),
+])
+def test_oproj_mlp_block_matches_chain_and_oracle(batch, d_attn, d, ff, dt):
+    from decodebench_b200 import ops
+
+    x, g, Wg, Wu, Wd, _ = _inputs(11 * batch + d, batch, d, ff, dt, True, False)
+    rng = np.random.default_rng(d_attn)
+    attn = bits(rng, (batch, d_attn), dt)
+    Wo = bits(rng, (d, d_attn), dt, 1 / 64)
+    tx, tg, tWg, tWu, tWd, ta, tWo = (_t(a, dt) for a in (x, g, Wg, Wu, Wd, attn, Wo))
+    ha = torch.empty(batch, d, dtype=tx.dtype, device="cuda")
+    h = torch.empty(batch, ff, dtype=tx.dtype, device="cuda")
+    y = ops.oproj_mlp_block(ta, tWo, tx, tWg, tWu, tWd, gamma=tg, eps=1e-5, h_attn=ha, h=h)
+    ops.check_device_error()
+
+    ha2 = ops.gemv(ta, tWo, residual=tx)
+    y2 = ops.mlp_block(ha2, tWg, tWu, tWd, gamma=tg, eps=1e-5, residual=ha2)
+    torch.cuda.synchronize()
+    assert torch.equal(ha, ha2), "h_attn differs from dbk_gemv"
+    assert torch.equal(y, y2), "y differs from dbk_gemv -> dbk_mlp_block"
+
+    ha_ref = O.gemv(attn, Wo, dt, residual=x)
+    assert_close(from_torch(ha), ha_ref, dt, "oproj_mlp_block h_attn")
+    y_ref = O.mlp(ha_ref, g, Wg, Wu, Wd, 1e-5, dt, residual=ha_ref)
+    assert_close(from_torch(y), y_ref, dt, "oproj_mlp_block y")
