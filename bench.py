@@ -2,7 +2,7 @@
 """Benchmark of the fused decode hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload f2|f1|f4|gqa|mlp|qkv|layer|f2fp8]
+                    [--workload f2|f1|f4|gqa|mlp|qkv|layer|f2fp8|mlpblock]
 
 The benchmark's five configs: C1 F1 RMSNorm -> GEMV 4096x4096 fp16; C2 F2
 gate+up -> SwiGLU, Wg/Wu [11008,4096] fp16; C3 F4 MHA FlashDecode, 32 heads x
@@ -955,8 +955,109 @@ class Layer(Workload):
         return self.cpu_rows * 4096 * 2
 
 
+class MLPBlock(Workload):
+    """The decode MLP block at batch 1 in one persistent launch (dbk_mlp_block):
+    RMSNorm -> gate/up [11008, 4096] -> SwiGLU -> grid barrier -> down [4096, 11008]
+    + residual, fp16 (C2's F2 followed by its down projection; the scope's next
+    rows, not a benchmark config). Single GPU."""
+
+    name = "mlpblock"
+    exchanges_per_step = 0
+
+    def __init__(self, rank, world, torch, d=4096, d_ff=11008, batch=1):
+        from decodebench_b200 import costs, ops
+
+        if world > 1:
+            raise SystemExit("the mlpblock workload runs on one GPU")
+        self.t, self.ops, self.costs = torch, ops, costs
+        self.rank, self.world, self.batch, self.d, self.d_ff = rank, world, batch, d, d_ff
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(77)
+        per_rep = 3 * d * d_ff * 2
+        self.nrep = max(2, math.ceil(2 * 126e6 / per_rep))
+
+        def w(r, c):
+            return (torch.randn(r, c, generator=g, device=dev) / math.sqrt(c)).half()
+        self.W = [(w(d_ff, d), w(d_ff, d), w(d, d_ff)) for _ in range(self.nrep)]
+        xg = torch.Generator().manual_seed(42)
+        self.x_cpu = torch.randn(batch, d, generator=xg).half()
+        self.x = self.x_cpu.to(dev)
+        self.gamma = (1 + 0.1 * torch.randn(d, generator=xg)).half().to(dev)
+        self.h = torch.empty(batch, d_ff, dtype=torch.float16, device=dev)
+        self.y = torch.empty(batch, d, dtype=torch.float16, device=dev)
+
+    def describe(self):
+        return {"workload": f"decode MLP block in one persistent launch: RMSNorm -> gate/up "
+                            f"[{self.d_ff},{self.d}] -> SwiGLU -> down [{self.d},{self.d_ff}] + "
+                            f"residual, x [{self.batch},{self.d}] fp16",
+                "global_batch": self.batch, "d_model": self.d, "d_ff": self.d_ff,
+                "parallelism": "single GPU", "weight_replicas": self.nrep,
+                "l2": f"weights rotated over {self.nrep} replicas "
+                      f"({self.nrep * 3 * self.d * self.d_ff * 2 / 1e6:.0f} MB > 126 MB L2)"}
+
+    def step_bytes_total(self):
+        # three weight matrices, x, gamma, y and the residual read (h stays on chip / in L2)
+        return self.costs.mlp_bytes(self.batch, self.d, self.d_ff) + 2 * self.batch * self.d
+
+    def launch_bytes(self):
+        return self.step_bytes_total()
+
+    def run_kernel(self, rep):
+        Wg, Wu, Wd = self.W[rep % self.nrep]
+        self.ops.mlp_block(self.x, Wg, Wu, Wd, gamma=self.gamma, eps=1e-5, residual=self.x,
+                           out=self.y, h=self.h)
+
+    def exchange(self):
+        pass
+
+    def torch_kernel(self, rep):
+        """Library baseline: the same block with PyTorch ops (cuBLAS GEMVs)."""
+        F = self.t.nn.functional
+        Wg, Wu, Wd = self.W[rep % self.nrep]
+        a = F.rms_norm(self.x, (self.d,), self.gamma, 1e-5)
+        return F.linear(F.silu(F.linear(a, Wg)) * F.linear(a, Wu), Wd) + self.x
+
+    def e2e_setup(self):
+        t = self.t
+        self.x_host = self.x_cpu.pin_memory()
+        self.out_host = t.empty(self.batch * self.d, dtype=t.float16).pin_memory()
+        self.x_dev = t.empty_like(self.x)
+        self._e2e_i = 0
+        return self.x_host.nbytes, self.out_host.nbytes
+
+    def e2e_step(self):
+        Wg, Wu, Wd = self.W[self._e2e_i % self.nrep]
+        self._e2e_i += 1
+        self.ops.stage(self.x_dev, self.x_host)
+        self.ops.mlp_block(self.x_dev, Wg, Wu, Wd, gamma=self.gamma, eps=1e-5,
+                           residual=self.x_dev, out=self.out_host.view(self.batch, -1), h=self.h)
+
+    def cpu_setup(self, frac_rows: float = 1.0):
+        import numpy as np
+
+        rng = np.random.default_rng(5)
+        n = max(1, int(self.d_ff * frac_rows))
+        self.cpu_rows = n
+        mk = lambda r, c: (rng.standard_normal((r, c), dtype=np.float32) / math.sqrt(c)  # noqa: E731
+                           ).astype(np.float16).astype(np.float32)
+        self.cWg, self.cWu = mk(n, self.d), mk(n, self.d)
+        self.cWd = mk(max(1, int(self.d * frac_rows)), n)
+        self.cx = self.x_cpu.float().numpy()[0].copy()
+
+    def cpu_step(self, threads):
+        from oracle import oracle as O
+
+        g = O.ref_gemv_threaded(self.cWg, self.cx, threads)
+        u = O.ref_gemv_threaded(self.cWu, self.cx, threads)
+        h = O.swiglu_f32(g, u, use_ref=True)
+        return O.ref_gemv_threaded(self.cWd, h, threads)
+
+    def cpu_step_bytes(self):
+        return 2 * (2 * self.cpu_rows * self.d + self.cWd.size)
+
+
 WORKLOADS = {"f2": F2, "f1": F1, "f4": F4, "gqa": GQA, "mlp": MLP, "qkv": QKV, "layer": Layer,
-             "f2fp8": F2FP8}
+             "f2fp8": F2FP8, "mlpblock": MLPBlock}
 
 
 # ---------------------------------------------------------------- timing
@@ -1376,6 +1477,12 @@ def _cpu_only_init(wl, name, torch):
                  if name == "f2" else "F1 RMSNorm -> GEMV, x [1,4096], W [4096,4096]")
         wl.describe_cpu = lambda: {"workload": label, "global_batch": 1, "d_in": 4096,
                                    "d_ff": wl.d_ff, "parallelism": "CPU host threads"}
+    elif name == "mlpblock":
+        wl.batch, wl.d, wl.d_ff = 1, 4096, 11008
+        wl.x_cpu = torch.randn(1, wl.d, generator=gen).half()
+        wl.describe_cpu = lambda: {"workload": "decode MLP block: gate/up [11008,4096] -> SwiGLU "
+                                               "-> down [4096,11008], x [1,4096] fp16",
+                                   "global_batch": 1, "parallelism": "CPU host threads"}
     else:
         wl.H, wl.L, wl.batch = 32, 4096, 1
         wl.describe_cpu = lambda: {"workload": "F4 MHA q [1,32,1,128], K/V [1,32,4096,128]",
