@@ -1104,7 +1104,7 @@ __device__ __forceinline__ bool grid_barrier(int* sync, int nblocks) {
 // variant (d_in <= 2 chunks); without it one chain, the order of its per-k-step
 // variant. With skip, stages are waited for and released without computing
 // (drains the ring after a failed barrier). False when a bounded wait gave up.
-template <typename T, int NMAT, bool TWO_CHAINS>
+template <typename T, int NMAT, bool TWO_CHAINS, bool CACHED = false>
 __device__ __forceinline__ bool mlp_consume(const GemvArgs& a, int2 rows, const uint8_t* ring,
                                             uint64_t* full, uint64_t* empty, int nst, int& j,
                                             float* part, int pc, const uint16_t* xs, bool packed,
@@ -1123,6 +1123,18 @@ __device__ __forceinline__ bool mlp_consume(const GemvArgs& a, int2 rows, const 
                                                 : xs + (size_t)(b_ok ? bn : 0) * a.d_in) + kq;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+  uint32_t bfrag[CACHED ? 2 : 1][16][2];
+  if constexpr (CACHED) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) {
+        const int col = c * kMmaKC + warp * 256 + kk * 16;
+        const bool ok = !skip && b_ok && c < a.nchunks && col < a.d_in;
+        bfrag[c][kk][0] = ok ? *reinterpret_cast<const uint32_t*>(xh + col) : 0u;
+        bfrag[c][kk][1] = ok ? *reinterpret_cast<const uint32_t*>(xh + col + 8) : 0u;
+      }
+  }
   for (int t = 0; t < nmt * a.nchunks; ++t, ++j) {
     const int s = j % nst;
     const int mt = t / a.nchunks, c = t - mt * a.nchunks;
@@ -1130,7 +1142,29 @@ __device__ __forceinline__ bool mlp_consume(const GemvArgs& a, int2 rows, const 
     const int seg = min(kMmaKC, a.d_in - col0);
     if (!mbar_wait(&full[s], (j / nst) & 1, kDevTimeoutFull)) return false;
     const uint32_t stage = smem_u32(ring + (size_t)s * kMmaStage) + a_lane_off;
-    if (!skip) {
+    if (skip) {
+    } else if constexpr (CACHED) {
+      auto run_stage = [&](const uint32_t (&bb)[16][2]) {
+#pragma unroll
+        for (int k4 = 0; k4 < 16; k4 += 4) {
+          uint32_t af[4][4];
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const int k = warp * 256 + (k4 + kk) * 16;
+            if (k < seg) ldsm_x4(stage + k * 2, af[kk]);
+          }
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const int k = warp * 256 + (k4 + kk) * 16;
+            if (k < seg)
+              Mma<T>::run((kk & 1) ? acc2 : acc, af[kk][0], af[kk][1], af[kk][2], af[kk][3],
+                          bb[k4 + kk][0], bb[k4 + kk][1]);
+          }
+        }
+      };
+      if (c == 0) run_stage(bfrag[0]);
+      else run_stage(bfrag[1]);
+    } else {
 #pragma unroll 4
       for (int kk = 0; kk < 16; ++kk) {
         const int k = warp * 256 + kk * 16;
@@ -1338,8 +1372,8 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_block_kernel(const MlpArgs m)
     }
     inv_rms[tid] = v;
   }
-  if (!mlp_consume<T, 2, true>(A, rows_a, ring, full, empty, nst, j, part, pc_a, xs, packed_a,
-                               skip))
+  if (!mlp_consume<T, 2, true, true>(A, rows_a, ring, full, empty, nst, j, part, pc_a, xs,
+                                     packed_a, skip))
     return;
   named_bar_sync(1, kConsumers);
   if (!skip) {
