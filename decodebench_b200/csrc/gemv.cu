@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
   // warp always multiplies the same 16 k-steps of each chunk, so its activation
   // fragments are loaded from shared memory once instead of once per m-tile.
   // (Not for the QKV epilogue, whose registers would then spill.)
-  const bool cache_b = MODE != MODE_QKV && !W8 && a.nchunks <= 2 && !(SPLIT && !packed);
+  const bool cache_b = !W8 && a.nchunks <= 2 && !(SPLIT && !packed);
   uint32_t bfrag[2][16][2];
 #pragma unroll
   for (int c = 0; c < 2; ++c)
@@ -524,17 +524,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const GemvArgs a)
       // The activation fragments of this warp's k-steps were loaded once (before
       // the loop); the weight loads of 8 k-steps are issued back to back before
       // their MMAs, which alternate between two accumulator chains.
+      // weight loads in batches of KB k-steps (4 for the QKV epilogue's registers)
+      constexpr int KB = MODE == MODE_QKV ? 4 : 8;
       auto run_stage = [&](const uint32_t (&bb)[16][2]) {
 #pragma unroll
-        for (int k8 = 0; k8 < 16; k8 += 8) {
-          uint32_t af[8][4];
+        for (int k8 = 0; k8 < 16; k8 += KB) {
+          uint32_t af[KB][4];
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
+          for (int kk = 0; kk < KB; ++kk) {
             const int k = warp * 256 + (k8 + kk) * 16;
             if (k < seg) ldsm_x4(stage + k * 2, af[kk]);
           }
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
+          for (int kk = 0; kk < KB; ++kk) {
             const int k = warp * 256 + (k8 + kk) * 16;
             if (k < seg)
               Mma<T>::run((kk & 1) ? acc2 : acc, af[kk][0], af[kk][1], af[kk][2], af[kk][3],
