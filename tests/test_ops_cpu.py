@@ -1,6 +1,7 @@
 """Host-side helpers of the added rows, on CPU tensors: the pair-interleaved
 Wqkv layout for dbk_qkv_rope_append, the rotary frequencies, and the per-row
-e4m3 quantisation for the fp8 GEMVs."""
+e4m3 quantisation for the fp8 GEMVs, and the choice between the persistent MLP
+block and two launches."""
 
 import pytest
 
@@ -41,3 +42,42 @@ def test_quantize_fp8_rows_bounds_the_error():
     rel = ((deq - W).abs() / W.abs().amax(dim=1, keepdim=True)).max()
     assert float(rel) <= 2 ** -4
     assert torch.allclose(deq.abs().amax(dim=1), W.abs().amax(dim=1), rtol=2 ** -4)
+
+
+def test_mlp_block_refuses_cpu_tensors():
+    t = lambda *s: torch.zeros(*s, dtype=torch.float16)  # noqa: E731
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ops.mlp_block(t(1, 256), t(4352, 256), t(4352, 256), t(256, 4352))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ops.oproj_mlp_block(t(1, 256), t(256, 256), t(1, 256), t(4352, 256), t(4352, 256),
+                            t(256, 4352))
+
+
+def test_mlp_takes_two_launches_when_the_single_launch_refuses(monkeypatch):
+    """ops.mlp: a DBK_ESHAPE answer of the persistent kernel (returned before any
+    launch) sends this shape to gate/up + down from then on; other errors raise."""
+    from decodebench_b200 import _native as N
+
+    calls = []
+
+    def refuse(*a, **k):
+        calls.append("block")
+        raise N.DbkError("dbk_mlp_block", N.DBK_ESHAPE)
+
+    monkeypatch.setattr(ops, "_MLP_BLOCK", True)
+    monkeypatch.setattr(ops, "_mlp_block_refused", set())
+    monkeypatch.setattr(ops, "mlp_block", refuse)
+    monkeypatch.setattr(ops, "gateup_swiglu", lambda x, *a, **k: calls.append("gateup") or x)
+    monkeypatch.setattr(ops, "gemv", lambda h, *a, **k: calls.append("gemv") or h)
+    x = torch.zeros(1, 64)
+    for _ in range(2):
+        ops.mlp(x, None, torch.zeros(300, 64), None, None)
+    assert calls == ["block", "gateup", "gemv", "gateup", "gemv"]
+
+    def broken(*a, **k):
+        raise N.DbkError("dbk_mlp_block", -3)       # DBK_EALIGN
+
+    monkeypatch.setattr(ops, "_mlp_block_refused", set())
+    monkeypatch.setattr(ops, "mlp_block", broken)
+    with pytest.raises(N.DbkError):
+        ops.mlp(x, None, torch.zeros(300, 64), None, None)
